@@ -1,0 +1,183 @@
+/*
+ * proteus_atlas.h — C ABI of the B200 (sm_100a) streaming-atlas kernels.
+ *
+ * Plain pointers and sizes only: every pointer is CUDA device memory unless stated otherwise, and
+ * every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream). The caller
+ * owns every buffer; no entry point allocates or frees device memory, and none keeps a pointer
+ * beyond the call. Return value: 0 on success, otherwise an ATLAS_ERR_* code with a message from
+ * atlas_last_error(). Data never raises an error: candidate-buffer overflow is reported through the
+ * device counters the reference uses (count > cap), exactly as filter_triton.py:66-68 does.
+ *
+ * Each entry point names the reference (haelyons/proteus) interface whose behaviour it provides.
+ * Layouts of the atlas state are the reference's (atlas/core.py:173-196):
+ *   top_s  f32 [G, K]   top_t i64 [G, K]   top_k i64 [G, K]   (G = L*2*D groups; sorted by top_k desc)
+ *   res_s  i64 [G*B, Kr] (= -key)  res_t i64 [G*B, Kr]  res_v f32 [G*B, Kr]   (sorted by res_s desc)
+ *   top_seed f32 [G]   res_seed i64 [G*B]   E f32 [L, 2, D, B]
+ */
+#ifndef PROTEUS_ATLAS_H
+#define PROTEUS_ATLAS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum atlas_dtype { ATLAS_F32 = 0, ATLAS_BF16 = 1, ATLAS_F16 = 2 };
+
+enum atlas_status {
+  ATLAS_OK = 0,
+  ATLAS_ERR_ARG = 1,      /* invalid argument (shape, stride, alignment, null pointer) */
+  ATLAS_ERR_CUDA = 2,     /* a CUDA runtime call or kernel launch failed */
+  ATLAS_ERR_UNSUPPORTED = 3
+};
+
+/* Message of the last error raised on the calling host thread ("" if none). */
+const char* atlas_last_error(void);
+/* ABI version of this library (bumped on any signature change). */
+int atlas_abi_version(void);
+
+/* ------------------------------------------------------------------------------------------------
+ * K1 compare-and-compact — replaces filter_candidates (atlas/filter_triton.py:65-86).
+ * survivor (t, d) <=> rowmap[t] >= 0 && (h > thr_pos[d] || -h > thr_neg[d]).
+ * H: [T, D] of `dtype` with row stride ld elements (unit column stride). rowmap i32 [T]: valid-row
+ * index or -1. Survivors are written as (val = h as fp32, row = rowmap[t], col = d) in arbitrary
+ * order into out_* [cap]; *count (must be 0 on entry) receives the exact survivor count even when it
+ * exceeds cap, and nothing is written past cap.
+ */
+int atlas_filter_compact(const void* H, int dtype, int64_t T, int64_t D, int64_t ld,
+                         const int32_t* rowmap, const float* thr_pos, const float* thr_neg,
+                         float* out_val, int32_t* out_row, int32_t* out_col, int32_t* count,
+                         int64_t cap, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Per-batch compaction thresholds — replaces the device math of Atlas.begin_batch
+ * (atlas/core.py:250-259):
+ *   tau_top = max(nextafter(top_s[g, K-1], -inf), top_seed[g])
+ *   kth     = max(res_s[g*B+b, Kr-1], res_seed[g*B+b]);  underfilled = kth < -U_res
+ *   eps     = nextafter(min_b{E[g, b] : underfilled}, -inf)  (inf when none)
+ *   thr[g]  = reservoir ? min(tau_top, eps) : tau_top            for g in [0, G)
+ */
+int atlas_thresholds(const float* top_s, int64_t K, const int64_t* res_s, int64_t Kr,
+                     const float* top_seed, const int64_t* res_seed, const float* E,
+                     int64_t G, int64_t B, int64_t U_res, int reservoir, float* thr, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Subsample row gathers — replace H.index_select(0, sub_rows) and Hn.index_select(0, res_in_sub)
+ * (atlas/core.py:289, :292).
+ * atlas_gather_transpose: XT[d, col0 + i] = H[rows[i], d] for i < n, zero for n <= i < round8(n);
+ *   XT has leading dimension ldx (elements, multiple of 8), same dtype as H.
+ * atlas_gather_rows: R[i, d] = H[rows[i], d] (R row stride D, same dtype as H).
+ */
+int atlas_gather_transpose(const void* H, int dtype, int64_t T, int64_t D, int64_t ld,
+                           const int32_t* rows, int64_t n, void* XT, int64_t ldx, int64_t col0,
+                           void* stream);
+int atlas_gather_rows(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, const int32_t* rows,
+                      int64_t n, void* R, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Subsample statistics — replaces sub_stats (atlas/stats_triton.py:163-203) and the accumulation
+ * of Atlas._subsample_stats_v3 / _v1 (atlas/core.py:312-338, :378-399).
+ * Input XT [D, n] (columns col0..col0+n of a transposed staging buffer, leading dim ldx).
+ * Accumulates in place, per column d:
+ *   sum[d] += sum_i x,  sq[d] += sum_i x^2          (fp32 within 8-row groups, fp64 across)
+ *   bins[(p*D + d)*B + b] += #{i : s_p >= E_p[d, b]} - #{i : s_p >= E_p[d, b+1]}   (int64; s_0 = x, s_1 = -x)
+ * and, when NL > 0, writes masks i8 [2, NL, D, n_pad]: masks[p, j, d, i] = (s_p >= E_p[d, levels[j]])
+ * for i < n, 0 for n <= i < n_pad (the layout of an exact int8 GEMM against [n_pad, A] one-hots).
+ * E0, E1: [D, B] fp32 (pole 0 / pole 1 lower edges). levels: host array of NL ints.
+ */
+int atlas_sub_stats(const void* XT, int dtype, int64_t ldx, int64_t col0, int64_t n, int64_t D,
+                    const float* E0, const float* E1, int64_t B, const int32_t* levels_host, int64_t NL,
+                    double* sum, double* sq, int64_t* bins, int8_t* masks, int64_t n_pad, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Exact int8 contingency GEMM on tcgen05 tensor cores — replaces _count_mm_i8 / torch._int_mm
+ * (atlas/core.py:762-774) and the accumulation enr[l] += c (core.py:398-399).
+ * masks i8 [M, n_pad] (row-major, K-major), annT i8 [A_pad, n_pad] (annotation one-hots transposed,
+ * zero padded), out i64 [M, A] accumulated in place: out[m, a] += sum_k masks[m, k] * annT[a, k].
+ * n_pad % 128 == 0, A_pad % 16 == 0, 16 <= A_pad <= 256, A <= A_pad, M % 128 == 0.
+ */
+int atlas_count_gemm_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int8_t* annT, int64_t A_pad,
+                        int64_t* out, int64_t A, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Upper-block-triangle Gram on tcgen05 tensor cores — replaces gram_accumulate
+ * (atlas/stats_triton.py:234-255): C[D, D] (fp32, row-major, contiguous) += X^T X on the 128x128
+ * blocks with block row <= block column; lower blocks untouched. X is supplied transposed:
+ * XT [D, n] bf16 or fp16 with leading dimension ldx (elements; ldx % 8 == 0, 16-byte aligned base).
+ */
+int atlas_gram_upper(const void* XT, int dtype, int64_t ldx, int64_t n, int64_t D, float* C, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Candidate admission for the filtered layers of a batch — replaces _merge_filtered_impl's
+ * candidate tests and the bulk-row paths _bulk_loop / _bulk_stacked (atlas/core.py:482-590).
+ * For every layer l with layer_mode[l] == 1 and count[l] <= cap(l):
+ *   compacted candidate (h, row, col), pole p (s = +-h), g = (l*2+p)*D + col:
+ *     top:  s > top_seed[g] && top_key(s, tok[row]) > top_k[g, K-1]      -> record (g, top_key, tok, s)
+ *     res:  b = bin(s, E[l,p,col]) >= 0 && key[row] >= U_res && -key > max(res_s[g*B+b, Kr-1], res_seed)
+ *                                                                        -> record (g*B+b, -key, tok, h)
+ *   bulk rows R[l] [n_r, D] (rows with key < U_res; bulk_vidx = their valid-row indices):
+ *     every (row, col, pole) with bin >= 0 and -key > max(res_s[.., Kr-1], res_seed) -> res record.
+ * cap(l) = l < early_layers ? cap_early : cap_main. Candidate buffers are [L, cand_stride].
+ * Records are appended to SoA lists (group i32, score i64, tok i64, val f32) with device counters
+ * n_top / n_res; an append past the list capacity sets err[0] and is dropped.
+ */
+int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t U_res, int reservoir,
+                const int8_t* layer_mode_host, const int32_t* count, int64_t cap_main, int64_t cap_early,
+                int64_t early_layers, const float* cand_val, const int32_t* cand_row, const int32_t* cand_col,
+                int64_t cand_stride, const int64_t* tok, const int64_t* key,
+                const void* R, int dtype, int64_t n_r, int64_t r_stride, const int32_t* bulk_vidx,
+                const float* top_seed, const int64_t* top_k, const int64_t* res_s, const int64_t* res_seed,
+                const float* E,
+                int32_t* top_g, int64_t* top_sc, int64_t* top_tok, float* top_val, int32_t* n_top, int64_t top_cap,
+                int32_t* res_g, int64_t* res_sc, int64_t* res_tok, float* res_val, int32_t* n_res, int64_t res_cap,
+                int32_t* err, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Dense burst path for one layer — replaces Atlas._dense (atlas/core.py:407-446) without a forward
+ * re-run: runs on the live hook output when force != 0 or *count > cap (the 0.5%-fill overflow of
+ * the compaction buffer), otherwise returns immediately on the device.
+ * Per column and pole it selects, from the n_v valid rows, the exact top-K by top_key (the only
+ * batch elements that can enter the state's top-K) and, per bin, the Kr smallest keys among rows in
+ * the bin under the bin's key ceiling; admitted records are appended to the same lists as
+ * atlas_admit. key_order: valid-row indices sorted by key ascending. scratch: device bytes,
+ * >= atlas_dense_scratch_bytes(n_v, D, B). flag[0] is set to 1 when the dense path ran.
+ */
+int64_t atlas_dense_scratch_bytes(int64_t n_v, int64_t D, int64_t B);
+int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, int64_t layer,
+                       const int32_t* valid_rows, int64_t n_v, const int64_t* tok, const int64_t* key,
+                       const int32_t* key_order, int64_t B, int64_t K, int64_t Kr, int reservoir,
+                       const float* top_seed, const int64_t* top_k, const int64_t* res_s, const int64_t* res_seed,
+                       const float* E, const int32_t* count, int64_t cap, int force,
+                       int32_t* top_g, int64_t* top_sc, int64_t* top_tok, float* top_val, int32_t* n_top, int64_t top_cap,
+                       int32_t* res_g, int64_t* res_sc, int64_t* res_tok, float* res_val, int32_t* n_res, int64_t res_cap,
+                       void* scratch, int64_t scratch_bytes, int32_t* flag, int32_t* err, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Exact grouped top-K merge — replaces grouped_merge (atlas/core.py:75-104).
+ * state_sc i64 [G, K] sorted descending with payloads state_tok i64 [G, K], state_val f32 [G, K];
+ * candidates: *n_dev records (g i32, sc i64, tok i64, val f32), n_max a host upper bound on *n_dev.
+ * Afterwards each touched row holds the K largest scores of (row U its candidates), descending,
+ * with their payloads. Scores must be unique within a group (the atlas keys are).
+ * Workspace (device): ws_i32 of atlas_merge_ws_i32(G, n_max) ints, ws_bytes of
+ * atlas_merge_ws_bytes(n_max) bytes.
+ */
+int64_t atlas_merge_ws_i32(int64_t G, int64_t n_max);
+int64_t atlas_merge_ws_bytes(int64_t n_max);
+int atlas_grouped_merge(int64_t* state_sc, int64_t* state_tok, float* state_val, int64_t G, int64_t K,
+                        const int32_t* g, const int64_t* sc, const int64_t* tok, const float* val,
+                        const int32_t* n_dev, int64_t n_max, int32_t* ws_i32, void* ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Row-wise merge of two sorted states — replaces the top-K / reservoir part of Atlas.merge_from
+ * (atlas/core.py:636-643): for each of G rows, (sc, tok, val) <- the K largest of
+ * (sc U other_sc) with payloads (keys unique across the two states).
+ */
+int atlas_merge_rows(int64_t* sc, int64_t* tok, float* val, const int64_t* other_sc, const int64_t* other_tok,
+                     const float* other_val, int64_t G, int64_t K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PROTEUS_ATLAS_H */

@@ -1,0 +1,189 @@
+// Candidate admission for the filtered layers of a batch (end of batch): the exact per-group tests
+// of _merge_filtered_impl (atlas/core.py:482-527) over the compacted candidates, and the bulk-row
+// reservoir path of _bulk_loop / _bulk_stacked (core.py:529-590) stacked over every layer in one
+// launch. Admitted records go to SoA lists through warp-aggregated appends (one atomic per warp
+// per step), ready for atlas_grouped_merge.
+#include "common.cuh"
+
+namespace atlas {
+namespace {
+
+struct Lists {
+  int32_t* tg; int64_t* tsc; int64_t* ttok; float* tval; int32_t* nt; int64_t tcap;
+  int32_t* rg; int64_t* rsc; int64_t* rtok; float* rval; int32_t* nr; int64_t rcap;
+  int32_t* err;
+};
+
+// Append up to 2 records per lane to one list; the whole warp calls this.
+__device__ __forceinline__ void warp_append(int lane, int n, const int32_t (&g)[2], const int64_t (&sc)[2],
+                                            const int64_t (&tok)[2], const float (&val)[2], int32_t* gl, int64_t* scl,
+                                            int64_t* tokl, float* vall, int32_t* counter, int64_t cap, int32_t* err) {
+  if (!__any_sync(0xFFFFFFFFu, n > 0)) return;
+  int total;
+  const int pre = warp_excl_scan(n, lane, &total);
+  int base = 0;
+  if (lane == 31) base = atomicAdd(counter, total);
+  base = __shfl_sync(0xFFFFFFFFu, base, 31);
+  for (int k = 0; k < n; ++k) {
+    const int64_t slot = (int64_t)base + pre + k;
+    if (slot < cap) {
+      gl[slot] = g[k];
+      scl[slot] = sc[k];
+      tokl[slot] = tok[k];
+      vall[slot] = val[k];
+    } else {
+      atomicExch(err, 1);
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_elem(const T* p) { return Elem<ATLAS_F32>::f(*p); }
+template <>
+__device__ __forceinline__ float ld_elem<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <>
+__device__ __forceinline__ float ld_elem<__half>(const __half* p) { return __half2float(*p); }
+
+template <typename RT>
+__global__ void __launch_bounds__(256)
+admit_kernel(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t U_res, int reservoir, uint64_t mode_mask,
+             const int32_t* __restrict__ count, int64_t cap_main, int64_t cap_early, int64_t early_layers,
+             const float* __restrict__ cval, const int32_t* __restrict__ crow, const int32_t* __restrict__ ccol,
+             int64_t cstride, const int64_t* __restrict__ tok, const int64_t* __restrict__ key,
+             const RT* __restrict__ R, int64_t n_r, int64_t r_stride, const int32_t* __restrict__ bulk_vidx,
+             const float* __restrict__ top_seed, const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
+             const int64_t* __restrict__ res_seed, const float* __restrict__ E, Lists o) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_id = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t l = 0; l < L; ++l) {
+    if (!((mode_mask >> l) & 1)) continue;
+    const int64_t cap = l < early_layers ? cap_early : cap_main;
+    const int64_t c = count[l];
+    if (c > cap) continue;  // overflowed: this layer went through the dense path
+    // ---- compacted candidates
+    for (int64_t base = warp_id * 32; base < c; base += n_warps * 32) {
+      const int64_t i = base + lane;
+      int nt = 0, nr = 0;
+      int32_t tg[2], rg[2];
+      int64_t tsc[2], rsc[2], tt[2], rt[2];
+      float tv[2], rv[2];
+      if (i < c) {
+        const float h = cval[l * cstride + i];
+        const int32_t row = crow[l * cstride + i];
+        const int64_t col = ccol[l * cstride + i];
+        const int64_t tk = tok[row], ky = key[row];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float s = p ? -h : h;
+          const int64_t g = (l * 2 + p) * D + col;
+          if (s > top_seed[g]) {
+            const int64_t k64 = top_key(s, tk);
+            if (k64 > top_k[g * K + (K - 1)]) {
+              tg[nt] = (int32_t)g; tsc[nt] = k64; tt[nt] = tk; tv[nt] = s; ++nt;
+            }
+          }
+          if (reservoir && ky >= U_res) {
+            const int b = bin_of(s, E + g * B, (int)B);
+            if (b >= 0) {
+              const int64_t gr = g * B + b;
+              int64_t thr = res_s[gr * Kr + (Kr - 1)];
+              const int64_t sd = res_seed[gr];
+              if (sd > thr) thr = sd;
+              if (-ky > thr) {
+                rg[nr] = (int32_t)gr; rsc[nr] = -ky; rt[nr] = tk; rv[nr] = h; ++nr;
+              }
+            }
+          }
+        }
+      }
+      warp_append(lane, nt, tg, tsc, tt, tv, o.tg, o.tsc, o.ttok, o.tval, o.nt, o.tcap, o.err);
+      warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
+    }
+    // ---- bulk rows (key < U_res): every element is a reservoir candidate
+    if (!reservoir || n_r == 0) continue;
+    const int64_t nb = n_r * D;
+    for (int64_t base = warp_id * 32; base < nb; base += n_warps * 32) {
+      const int64_t e = base + lane;
+      int nr = 0;
+      int32_t rg[2];
+      int64_t rsc[2], rt[2];
+      float rv[2];
+      if (e < nb) {
+        const int64_t i = e / D, col = e - i * D;
+        const float h = ld_elem<RT>(R + (l * r_stride + i) * D + col);
+        const int32_t vi = bulk_vidx[i];
+        const int64_t tk = tok[vi], ky = key[vi];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const float s = p ? -h : h;
+          const int64_t g = (l * 2 + p) * D + col;
+          const int b = bin_of(s, E + g * B, (int)B);
+          if (b >= 0) {
+            const int64_t gr = g * B + b;
+            int64_t thr = res_s[gr * Kr + (Kr - 1)];
+            const int64_t sd = res_seed[gr];
+            if (sd > thr) thr = sd;
+            if (-ky > thr) {
+              rg[nr] = (int32_t)gr; rsc[nr] = -ky; rt[nr] = tk; rv[nr] = h; ++nr;
+            }
+          }
+        }
+      }
+      warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace atlas
+
+using namespace atlas;
+
+extern "C" int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t U_res, int reservoir,
+                           const int8_t* layer_mode_host, const int32_t* count, int64_t cap_main, int64_t cap_early,
+                           int64_t early_layers, const float* cand_val, const int32_t* cand_row, const int32_t* cand_col,
+                           int64_t cand_stride, const int64_t* tok, const int64_t* key, const void* R, int dtype,
+                           int64_t n_r, int64_t r_stride, const int32_t* bulk_vidx, const float* top_seed,
+                           const int64_t* top_k, const int64_t* res_s, const int64_t* res_seed, const float* E,
+                           int32_t* top_g, int64_t* top_sc, int64_t* top_tok, float* top_val, int32_t* n_top,
+                           int64_t top_cap, int32_t* res_g, int64_t* res_sc, int64_t* res_tok, float* res_val,
+                           int32_t* n_res, int64_t res_cap, int32_t* err, void* stream) {
+  ATLAS_REQUIRE(L >= 0 && L <= 64, "admit: L must be 0..64");
+  ATLAS_REQUIRE(D > 0 && B >= 1 && K >= 1 && Kr >= 1 && n_r >= 0 && r_stride >= n_r, "admit: bad sizes");
+  ATLAS_REQUIRE(2 * L * D * B < (1LL << 31), "admit: group ids exceed int32");
+  uint64_t mask = 0;
+  for (int64_t l = 0; l < L; ++l)
+    if (layer_mode_host && layer_mode_host[l]) mask |= 1ull << l;
+  if (mask == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(count && cand_val && cand_row && cand_col && tok && key && top_seed && top_k && n_top && top_g &&
+                    top_sc && top_tok && top_val && err,
+                "admit: null pointer");
+  ATLAS_REQUIRE(!reservoir || (res_s && res_seed && E && res_g && res_sc && res_tok && res_val && n_res),
+                "admit: null reservoir pointer");
+  ATLAS_REQUIRE(!reservoir || n_r == 0 || (R && bulk_vidx), "admit: bulk rows missing");
+  Lists o{top_g, top_sc, top_tok, top_val, n_top, top_cap, res_g, res_sc, res_tok, res_val, n_res, res_cap, err};
+  const int64_t work = (cap_main > cap_early ? cap_main : cap_early) + n_r * D;
+  const unsigned grid = grid_for(work, 256, 8);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case ATLAS_BF16:
+      admit_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(L, D, B, K, Kr, U_res, reservoir, mask, count, cap_main, cap_early,
+          early_layers, cand_val, cand_row, cand_col, cand_stride, tok, key, (const __nv_bfloat16*)R, n_r, r_stride,
+          bulk_vidx, top_seed, top_k, res_s, res_seed, E, o);
+      break;
+    case ATLAS_F16:
+      admit_kernel<__half><<<grid, 256, 0, st>>>(L, D, B, K, Kr, U_res, reservoir, mask, count, cap_main, cap_early,
+          early_layers, cand_val, cand_row, cand_col, cand_stride, tok, key, (const __half*)R, n_r, r_stride, bulk_vidx,
+          top_seed, top_k, res_s, res_seed, E, o);
+      break;
+    case ATLAS_F32:
+      admit_kernel<float><<<grid, 256, 0, st>>>(L, D, B, K, Kr, U_res, reservoir, mask, count, cap_main, cap_early,
+          early_layers, cand_val, cand_row, cand_col, cand_stride, tok, key, (const float*)R, n_r, r_stride, bulk_vidx,
+          top_seed, top_k, res_s, res_seed, E, o);
+      break;
+    default:
+      return fail(ATLAS_ERR_ARG, "admit: unknown dtype %d", dtype);
+  }
+  return check_launch("atlas_admit");
+}

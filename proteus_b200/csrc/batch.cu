@@ -1,0 +1,290 @@
+// Per-batch helpers: compaction thresholds (begin_batch), subsample row gathers, and the
+// subsample-statistics kernel (bin masses, moments, int8 enrichment masks).
+#include "common.cuh"
+
+namespace atlas {
+namespace {
+
+// ---------------------------------------------------------------------------- thresholds
+// One thread per (layer, pole, column) group; reads the K-th slot of the top-K state and the Kr-th
+// slot of the B reservoirs (core.py:250-259).
+__global__ void thresholds_kernel(const float* __restrict__ top_s, int64_t K, const int64_t* __restrict__ res_s,
+                                  int64_t Kr, const float* __restrict__ top_seed, const int64_t* __restrict__ res_seed,
+                                  const float* __restrict__ E, int64_t G, int64_t B, int64_t U_res, int reservoir,
+                                  float* __restrict__ thr) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < G; g += (int64_t)gridDim.x * blockDim.x) {
+    const float tau = top_s[g * K + (K - 1)];
+    const float tau_top = fmaxf(next_down(tau), top_seed[g]);
+    if (!reservoir) {
+      thr[g] = tau_top;
+      continue;
+    }
+    float eps = __int_as_float(0x7F800000);
+    for (int64_t b = 0; b < B; ++b) {
+      const int64_t gb = g * B + b;
+      int64_t kth = res_s[gb * Kr + (Kr - 1)];
+      const int64_t sd = res_seed[gb];
+      if (sd > kth) kth = sd;
+      if (kth < -U_res) eps = fminf(eps, E[gb]);
+    }
+    thr[g] = fminf(tau_top, next_down(eps));
+  }
+}
+
+// ---------------------------------------------------------------------------- gathers
+// XT[d, col0 + i] = H[rows[i], d]: 32x32 tiles through shared memory (coalesced on both sides).
+template <typename T>
+__global__ void gather_transpose_kernel(const T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
+                                        int64_t n, int64_t n8, T* __restrict__ XT, int64_t ldx, int64_t col0) {
+  __shared__ T tile[32][33];
+  const int64_t i0 = (int64_t)blockIdx.x * 32;
+  const int64_t d0 = (int64_t)blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int k = ty; k < 32; k += 8) {
+    const int64_t i = i0 + k, d = d0 + tx;
+    T v = T(0.0f);
+    if (i < n && d < D) v = H[(int64_t)rows[i] * ld + d];
+    tile[k][tx] = v;
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {
+    const int64_t d = d0 + k, i = i0 + tx;
+    if (d < D && i < n8) XT[d * ldx + col0 + i] = tile[tx][k];
+  }
+}
+
+template <typename T>
+__global__ void gather_rows_kernel(const T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
+                                   int64_t n, T* __restrict__ R) {
+  const int64_t total = n * D;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / D, d = e - i * D;
+    R[e] = H[(int64_t)rows[i] * ld + d];
+  }
+}
+
+__global__ void gather_rows_vec_kernel(const uint4* __restrict__ H, int64_t Dv, int64_t ldv, const int32_t* __restrict__ rows,
+                                       int64_t n, uint4* __restrict__ R) {
+  const int64_t total = n * Dv;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / Dv, d = e - i * Dv;
+    R[e] = H[(int64_t)rows[i] * ldv + d];
+  }
+}
+
+// ---------------------------------------------------------------------------- subsample statistics
+// One warp per column d; each lane takes 8 consecutive subsample rows per step (one 16-byte vector
+// of XT for 16-bit types). Bin counts use the cumulative form of the reference's v1 path
+// (#{s >= E_b} differences, core.py:322-327); masks are (s >= E[lev]) (core.py:329).
+constexpr int kMaxB = 8;
+constexpr int kMaxNL = 8;
+
+struct Levels {
+  int v[kMaxNL];
+};
+
+template <int DT>
+__device__ __forceinline__ void load8(const typename Elem<DT>::T* p, int64_t i, int64_t n, float (&x)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) x[k] = (i + k < n) ? Elem<DT>::f(p[k]) : 0.0f;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256)
+sub_stats_kernel(const typename Elem<DT>::T* __restrict__ XT, int64_t ldx, int64_t col0, int64_t n, int64_t D,
+                 const float* __restrict__ E0, const float* __restrict__ E1, int B, Levels lev, int NL,
+                 double* __restrict__ sum, double* __restrict__ sq, int64_t* __restrict__ bins,
+                 int8_t* __restrict__ masks, int64_t n_pad) {
+  const int lane = threadIdx.x & 31;
+  const int64_t d = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (d >= D) return;
+  float e0[kMaxB], e1[kMaxB];
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) {
+    e0[b] = b < B ? E0[d * B + b] : __int_as_float(0x7F800000);
+    e1[b] = b < B ? E1[d * B + b] : __int_as_float(0x7F800000);
+  }
+  float m0[kMaxNL], m1[kMaxNL];
+#pragma unroll
+  for (int j = 0; j < kMaxNL; ++j) {
+    m0[j] = j < NL ? E0[d * B + lev.v[j]] : 0.0f;
+    m1[j] = j < NL ? E1[d * B + lev.v[j]] : 0.0f;
+  }
+  int c0[kMaxB], c1[kMaxB];
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) c0[b] = c1[b] = 0;
+  double acc_s = 0.0, acc_q = 0.0;
+  const typename Elem<DT>::T* col = XT + d * ldx + col0;
+  const int64_t n_loop = masks ? n_pad : n;
+  for (int64_t i = (int64_t)lane * 8; i < n_loop; i += 256) {
+    float x[8];
+    load8<DT>(col + i, i, n, x);
+    float s32 = 0.0f, q32 = 0.0f;
+    uint32_t valid = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const bool v = i + k < n;
+      valid |= (v ? 1u : 0u) << k;
+      s32 += x[k];
+      q32 = fmaf(x[k], x[k], q32);
+#pragma unroll
+      for (int b = 0; b < kMaxB; ++b) {
+        c0[b] += (v && x[k] >= e0[b]) ? 1 : 0;
+        c1[b] += (v && -x[k] >= e1[b]) ? 1 : 0;
+      }
+    }
+    acc_s += (double)s32;
+    acc_q += (double)q32;
+    if (masks) {
+#pragma unroll
+      for (int j = 0; j < kMaxNL; ++j) {
+        if (j >= NL) break;
+        uint64_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (valid & (1u << k)) {
+            w0 |= (uint64_t)(x[k] >= m0[j] ? 1 : 0) << (8 * k);
+            w1 |= (uint64_t)(-x[k] >= m1[j] ? 1 : 0) << (8 * k);
+          }
+        }
+        *reinterpret_cast<uint64_t*>(masks + ((int64_t)(0 * NL + j) * D + d) * n_pad + i) = w0;
+        *reinterpret_cast<uint64_t*>(masks + ((int64_t)(1 * NL + j) * D + d) * n_pad + i) = w1;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc_s += __shfl_xor_sync(0xFFFFFFFFu, acc_s, o);
+    acc_q += __shfl_xor_sync(0xFFFFFFFFu, acc_q, o);
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      c0[b] += __shfl_xor_sync(0xFFFFFFFFu, c0[b], o);
+      c1[b] += __shfl_xor_sync(0xFFFFFFFFu, c1[b], o);
+    }
+  }
+  if (lane == 0) {
+    sum[d] += acc_s;
+    sq[d] += acc_q;
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      if (b >= B) break;
+      const int nx0 = (b + 1 < B) ? c0[b + 1] : 0;
+      const int nx1 = (b + 1 < B) ? c1[b + 1] : 0;
+      bins[d * B + b] += (int64_t)(c0[b] - nx0);
+      bins[(D + d) * B + b] += (int64_t)(c1[b] - nx1);
+    }
+  }
+}
+
+template <int DT>
+int launch_stats(const void* XT, int64_t ldx, int64_t col0, int64_t n, int64_t D, const float* E0, const float* E1,
+                 int64_t B, const Levels& lev, int64_t NL, double* sum, double* sq, int64_t* bins, int8_t* masks,
+                 int64_t n_pad, cudaStream_t st) {
+  const int warps = 8;
+  dim3 grid((unsigned)((D + warps - 1) / warps));
+  sub_stats_kernel<DT><<<grid, warps * 32, 0, st>>>(reinterpret_cast<const typename Elem<DT>::T*>(XT), ldx, col0, n, D,
+                                                     E0, E1, (int)B, lev, (int)NL, sum, sq, bins, masks, n_pad);
+  return check_launch("atlas_sub_stats");
+}
+
+int esize(int dtype) { return dtype == ATLAS_F32 ? 4 : 2; }
+
+}  // namespace
+}  // namespace atlas
+
+using namespace atlas;
+
+extern "C" int atlas_thresholds(const float* top_s, int64_t K, const int64_t* res_s, int64_t Kr, const float* top_seed,
+                                const int64_t* res_seed, const float* E, int64_t G, int64_t B, int64_t U_res,
+                                int reservoir, float* thr, void* stream) {
+  ATLAS_REQUIRE(K >= 1 && Kr >= 1 && G >= 0 && B >= 1, "thresholds: bad sizes K=%lld Kr=%lld G=%lld B=%lld",
+                (long long)K, (long long)Kr, (long long)G, (long long)B);
+  if (G == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(top_s && top_seed && thr && (!reservoir || (res_s && res_seed && E)), "thresholds: null pointer");
+  thresholds_kernel<<<grid_for(G, 256), 256, 0, (cudaStream_t)stream>>>(top_s, K, res_s, Kr, top_seed, res_seed, E, G,
+                                                                        B, U_res, reservoir, thr);
+  return check_launch("atlas_thresholds");
+}
+
+extern "C" int atlas_gather_transpose(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, const int32_t* rows,
+                                      int64_t n, void* XT, int64_t ldx, int64_t col0, void* stream) {
+  ATLAS_REQUIRE(T >= 0 && D >= 0 && ld >= D && n >= 0 && col0 >= 0, "gather_transpose: bad sizes");
+  const int64_t n8 = (n + 7) / 8 * 8;
+  ATLAS_REQUIRE(col0 + n8 <= ldx, "gather_transpose: columns %lld..%lld exceed ldx %lld", (long long)col0,
+                (long long)(col0 + n8), (long long)ldx);
+  if (n8 == 0 || D == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(H && rows && XT, "gather_transpose: null pointer");
+  dim3 grid((unsigned)((n8 + 31) / 32), (unsigned)((D + 31) / 32));
+  ATLAS_REQUIRE(grid.y < 65536, "gather_transpose: D too large");
+  dim3 block(32, 8);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case ATLAS_BF16:
+      gather_transpose_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)H, D, ld, rows, n, n8,
+                                                                      (__nv_bfloat16*)XT, ldx, col0);
+      break;
+    case ATLAS_F16:
+      gather_transpose_kernel<__half><<<grid, block, 0, st>>>((const __half*)H, D, ld, rows, n, n8, (__half*)XT, ldx, col0);
+      break;
+    case ATLAS_F32:
+      gather_transpose_kernel<float><<<grid, block, 0, st>>>((const float*)H, D, ld, rows, n, n8, (float*)XT, ldx, col0);
+      break;
+    default:
+      return fail(ATLAS_ERR_ARG, "gather_transpose: unknown dtype %d", dtype);
+  }
+  return check_launch("atlas_gather_transpose");
+}
+
+extern "C" int atlas_gather_rows(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, const int32_t* rows,
+                                 int64_t n, void* R, void* stream) {
+  ATLAS_REQUIRE(T >= 0 && D >= 0 && ld >= D && n >= 0, "gather_rows: bad sizes");
+  if (n == 0 || D == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(H && rows && R, "gather_rows: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int es = esize(dtype);
+  if ((D * es) % 16 == 0 && (ld * es) % 16 == 0 && (uintptr_t)H % 16 == 0 && (uintptr_t)R % 16 == 0) {
+    const int64_t Dv = D * es / 16, ldv = ld * es / 16;
+    gather_rows_vec_kernel<<<grid_for(n * Dv, 256), 256, 0, st>>>((const uint4*)H, Dv, ldv, rows, n, (uint4*)R);
+    return check_launch("atlas_gather_rows");
+  }
+  switch (dtype) {
+    case ATLAS_BF16:
+    case ATLAS_F16:
+      gather_rows_kernel<uint16_t><<<grid_for(n * D, 256), 256, 0, st>>>((const uint16_t*)H, D, ld, rows, n, (uint16_t*)R);
+      break;
+    case ATLAS_F32:
+      gather_rows_kernel<float><<<grid_for(n * D, 256), 256, 0, st>>>((const float*)H, D, ld, rows, n, (float*)R);
+      break;
+    default:
+      return fail(ATLAS_ERR_ARG, "gather_rows: unknown dtype %d", dtype);
+  }
+  return check_launch("atlas_gather_rows");
+}
+
+extern "C" int atlas_sub_stats(const void* XT, int dtype, int64_t ldx, int64_t col0, int64_t n, int64_t D,
+                               const float* E0, const float* E1, int64_t B, const int32_t* levels_host, int64_t NL,
+                               double* sum, double* sq, int64_t* bins, int8_t* masks, int64_t n_pad, void* stream) {
+  ATLAS_REQUIRE(n >= 0 && D >= 0 && B >= 1 && B <= kMaxB, "sub_stats: bad sizes (B must be 1..%d)", kMaxB);
+  ATLAS_REQUIRE(NL >= 0 && NL <= kMaxNL, "sub_stats: NL must be 0..%d", kMaxNL);
+  if (D == 0 || n == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(XT && E0 && E1 && sum && sq && bins, "sub_stats: null pointer");
+  ATLAS_REQUIRE(col0 % 8 == 0 && ldx % 8 == 0 && col0 + n <= ldx, "sub_stats: col0/ldx must be multiples of 8");
+  Levels lev{};
+  for (int j = 0; j < NL; ++j) {
+    ATLAS_REQUIRE(levels_host && levels_host[j] >= 0 && levels_host[j] < B, "sub_stats: level %d out of range", j);
+    lev.v[j] = levels_host[j];
+  }
+  if (NL > 0) {
+    ATLAS_REQUIRE(masks != nullptr, "sub_stats: masks required when NL > 0");
+    ATLAS_REQUIRE(n_pad >= n && n_pad % 8 == 0 && (uintptr_t)masks % 8 == 0, "sub_stats: bad n_pad / mask alignment");
+  } else {
+    masks = nullptr;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case ATLAS_BF16: return launch_stats<ATLAS_BF16>(XT, ldx, col0, n, D, E0, E1, B, lev, NL, sum, sq, bins, masks, n_pad, st);
+    case ATLAS_F16: return launch_stats<ATLAS_F16>(XT, ldx, col0, n, D, E0, E1, B, lev, NL, sum, sq, bins, masks, n_pad, st);
+    case ATLAS_F32: return launch_stats<ATLAS_F32>(XT, ldx, col0, n, D, E0, E1, B, lev, NL, sum, sq, bins, masks, n_pad, st);
+    default: return fail(ATLAS_ERR_ARG, "sub_stats: unknown dtype %d", dtype);
+  }
+}

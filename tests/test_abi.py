@@ -1,0 +1,49 @@
+"""CPU checks of the C ABI boundary: the in-tree library loads and exports every symbol that
+include/proteus_atlas.h declares, with the binding derived from the header (no compute calls)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+from proteus_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_header_declares_and_library_exports_every_symbol():
+    lib = _lib.load()
+    names = set(_lib.SIGNATURES)
+    text = (ROOT / "include" / "proteus_atlas.h").read_text()
+    declared = set(re.findall(r"\b(atlas_\w+)\s*\(", re.sub(r"/\*.*?\*/", " ", text, flags=re.S)))
+    assert declared == names, declared ^ names
+    for n in names:
+        assert hasattr(lib, n), n
+    assert lib.atlas_abi_version() >= 1
+
+
+def test_argument_errors_are_reported_without_a_gpu():
+    lib = _lib.load()
+    # T < 0 is rejected on the host before any CUDA call
+    rc = lib.atlas_filter_compact(None, 1, -1, 8, 8, None, None, None, None, None, None, None, 0, None)
+    assert rc == 1
+    assert b"bad shape" in lib.atlas_last_error()
+    rc = lib.atlas_grouped_merge(None, None, None, 10, 300, None, None, None, None, None, 5, None, None, None)
+    assert rc == 1 and b"K must be" in lib.atlas_last_error()
+
+
+def test_workspace_size_queries():
+    lib = _lib.load()
+    assert lib.atlas_merge_ws_i32(4096, 100) >= 4 * 4096
+    assert lib.atlas_merge_ws_bytes(1000) >= 20 * 1000
+    assert lib.atlas_dense_scratch_bytes(32768, 5120, 5) == 64 * 2 * 5 * 5120 * 4
+
+
+def test_product_refuses_cpu_device():
+    import pytest
+    import torch
+
+    from proteus_b200.core import Atlas, AtlasConfig
+    from proteus_b200._lib import AtlasKernelError
+    with pytest.raises(AtlasKernelError):
+        Atlas(1, 8, torch.zeros(1, 2, 8, 5), AtlasConfig(), device="cpu")

@@ -1,0 +1,169 @@
+"""Kernel-level parity on the GPU: each sm_100a kernel against the reference's own outputs
+(tests/golden/*.npz) or, for floating-point contractions, an fp64 truth with a stated tolerance."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from tests.harness import golden
+from tests.streams import FILTER_CASES, STATS_CASES, filter_inputs, stats_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _kn():
+    from proteus_b200 import kernels
+    return kernels
+
+
+@pytest.mark.parametrize("case", range(len(FILTER_CASES)))
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_filter_matches_reference(case, dtype):
+    """Survivor set, values and count of filter_candidates (filter_triton.py:65-86) — bit-exact,
+    including the exact count when the output buffer overflows (cap 64)."""
+    KN = _kn()
+    H, rowmap, tp, tn = filter_inputs(case)
+    Hd = torch.from_numpy(H).to(DEV).to(dtype)
+    rm = torch.from_numpy(rowmap).to(DEV)
+    tpd, tnd = torch.from_numpy(tp).to(DEV), torch.from_numpy(tn).to(DEV)
+    v, r, c, cnt = KN.filter_candidates(Hd, rm, tpd, tnd, 1 << 16)
+    n = int(cnt)
+    if dtype == torch.bfloat16:  # the golden is the reference kernel on these bf16 inputs
+        z = golden("filter")
+        assert n == int(z[f"f{case}_count"])
+        o = np.lexsort((c[:n].cpu().numpy(), r[:n].cpu().numpy()))
+        assert np.array_equal(r[:n].cpu().numpy()[o], z[f"f{case}_row"])
+        assert np.array_equal(c[:n].cpu().numpy()[o], z[f"f{case}_col"])
+        assert np.array_equal(v[:n].cpu().numpy()[o], z[f"f{case}_val"])
+    Hf = H.astype(np.float32)
+    want = ((Hf > tp) | (-Hf > tn)) & (rowmap >= 0)[:, None]
+    assert n == int(want.sum())
+    _, _, _, cnt64 = KN.filter_candidates(Hd, rm, tpd, tnd, 64)
+    assert int(cnt64) == n  # overflow: exact count, nothing past cap
+
+
+def test_filter_large_vector_path():
+    """bf16 16-byte vector path at a B200-sized shape with a padding mix and -inf thresholds."""
+    KN = _kn()
+    g = torch.Generator(device=DEV).manual_seed(0)
+    T, D = 4099, 5120
+    H = (torch.randn(T, D, generator=g, device=DEV) * 2).to(torch.bfloat16)
+    valid = torch.rand(T, generator=g, device=DEV) > 0.1
+    rowmap = torch.full((T,), -1, dtype=torch.int64, device=DEV)
+    rowmap[valid] = torch.arange(int(valid.sum()), device=DEV)
+    tp = torch.rand(D, generator=g, device=DEV) + 5.0
+    tn = torch.rand(D, generator=g, device=DEV) + 5.0
+    tn[:3] = float("-inf")
+    v, r, c, cnt = KN.filter_candidates(H, rowmap, tp, tn, 1 << 20)
+    n = int(cnt)
+    Hf = H.float()
+    mask = ((Hf > tp) | (-Hf > tn)) & valid[:, None]
+    rt, ct = torch.nonzero(mask, as_tuple=True)
+    assert n == rt.numel()
+    got = torch.stack([r[:n], c[:n]], 1)
+    want = torch.stack([rowmap[rt], ct], 1)
+    key = lambda x: (x[:, 0] * D + x[:, 1]).sort().values  # noqa: E731
+    assert torch.equal(key(got), key(want))
+    inv = torch.nonzero(valid).squeeze(1)
+    assert torch.equal(v[:n], Hf[inv[r[:n]], c[:n]])
+
+
+@pytest.mark.parametrize("case", range(len(STATS_CASES)))
+def test_sub_stats_matches_reference(case):
+    """Bin masses and int8 masks bit-exact vs the reference kernel; sums within rtol 1e-5 (the
+    reference test's tolerance, tests/test_stats_triton.py:45-46)."""
+    KN = _kn()
+    X, E0, E1, levels = stats_inputs(case)
+    s, sq, cnt, M = KN.sub_stats(torch.from_numpy(X).to(DEV).to(torch.bfloat16), torch.from_numpy(E0).to(DEV),
+                                 torch.from_numpy(E1).to(DEV), levels)
+    z = golden("sub_stats")
+    if f"s{case}_cnt" in z:
+        assert np.array_equal(cnt.cpu().numpy(), z[f"s{case}_cnt"])
+        assert np.array_equal(M.cpu().numpy(), z[f"s{case}_M"])
+        assert np.allclose(s.cpu().numpy(), z[f"s{case}_sum"], rtol=1e-5, atol=1e-4)
+        assert np.allclose(sq.cpu().numpy(), z[f"s{case}_sq"], rtol=1e-5, atol=1e-4)
+    Xd = X.astype(np.float64)  # fp32 within 8-row groups, fp64 across: error far below 1e-6 of sum|x|
+    assert (np.abs(s.cpu().numpy() - Xd.sum(0)) <= 1e-6 * np.abs(Xd).sum(0) + 1e-12).all()
+    assert (np.abs(sq.cpu().numpy() - (Xd ** 2).sum(0)) <= 1e-6 * (Xd ** 2).sum(0) + 1e-12).all()
+
+
+@pytest.mark.parametrize("n,D", [(1600, 5120), (301, 1000), (77, 96), (4096, 640)])
+def test_gram_upper_blocks(n, D):
+    """gram_accumulate semantics: two accumulations, rel-max error < 1e-5 vs fp64 (reference
+    test tolerance, tests/test_stats_triton.py:74), lower 128-blocks untouched."""
+    KN = _kn()
+    g = torch.Generator().manual_seed(1)
+    X1 = torch.randn(n, D, generator=g).to(torch.bfloat16)
+    X2 = torch.randn(n // 2 + 3, D, generator=g).to(torch.bfloat16)
+    C = torch.zeros(D, D, device=DEV)
+    KN.gram_accumulate(X1.to(DEV), C)
+    KN.gram_accumulate(X2.to(DEV), C)
+    from proteus_b200.core import symmetrize_upper
+    G = symmetrize_upper(C.cpu().double())
+    R = X1.double().T @ X1.double() + X2.double().T @ X2.double()
+    rel = float((G - R).abs().max() / R.abs().max())
+    assert rel < 1e-5, rel
+    nb = -(-D // 128)
+    Cc = C.cpu()
+    for i in range(nb):
+        for j in range(i):
+            assert bool((Cc[i * 128:(i + 1) * 128, j * 128:(j + 1) * 128] == 0).all())
+
+
+@pytest.mark.parametrize("M,n,A", [(30720 // 8, 1664, 21), (768, 128, 16), (384, 2048, 48)])
+def test_count_gemm_i8_exact(M, n, A):
+    KN = _kn()
+    g = torch.Generator().manual_seed(2)
+    masks = (torch.rand(M, n, generator=g) < 0.3).to(torch.int8)
+    A_pad = max(16, -(-A // 16) * 16)
+    annT = torch.zeros(A_pad, n, dtype=torch.int8)
+    annT[:A] = (torch.rand(A, n, generator=g) < 0.2).to(torch.int8)
+    out = torch.full((M, A), 7, dtype=torch.int64, device=DEV)
+    KN.count_gemm_i8(masks.to(DEV), annT.to(DEV), out, A)
+    want = masks.long() @ annT[:A].long().T + 7
+    assert torch.equal(out.cpu(), want)
+
+
+def test_grouped_merge_matches_reference():
+    KN = _kn()
+    z = golden("grouped_merge")
+    I64_MIN = torch.iinfo(torch.int64).min
+    for case in range(3):
+        G, K, rounds = (int(x) for x in z[f"c{case}_meta"])
+        st = torch.full((G, K), I64_MIN, dtype=torch.long, device=DEV)
+        pt = torch.full((G, K), -1, dtype=torch.long, device=DEV)
+        pv = torch.full((G, K), float("-inf"), device=DEV)
+        for r in range(rounds):
+            t = lambda k: torch.from_numpy(z[f"c{case}_r{r}_{k}"]).to(DEV)  # noqa: E731
+            KN.grouped_merge(st, [pt, pv], t("g"), t("s"), [t("t"), t("v")], K)
+        assert np.array_equal(st.cpu().numpy(), z[f"c{case}_state"])
+        assert np.array_equal(pt.cpu().numpy(), z[f"c{case}_tok"])
+        assert np.array_equal(pv.cpu().numpy(), z[f"c{case}_val"])
+
+
+def test_grouped_merge_large_random_vs_oracle():
+    """Many candidates per group (several 32-wide chunks), K=100, against the oracle's merge."""
+    from oracle import atlas_np as O
+    KN = _kn()
+    rng = np.random.default_rng(3)
+    G, K = 500, 100
+    st = np.full((G, K), O.I64_MIN, np.int64)
+    pt = np.full((G, K), -1, np.int64)
+    pv = np.full((G, K), -np.inf, np.float32)
+    dst = torch.from_numpy(st).to(DEV)
+    dpt = torch.from_numpy(pt).to(DEV)
+    dpv = torch.from_numpy(pv).to(DEV)
+    for rnd in range(4):
+        n = 40000
+        g = rng.integers(0, G, n)
+        sc = rng.choice(2**50, n, replace=False).astype(np.int64) - 2**49
+        tok = rng.integers(0, 2**32, n)
+        val = rng.standard_normal(n).astype(np.float32)
+        O.grouped_merge(st, [pt, pv], g, sc, [tok, val], K, pay_fill=[-1, -np.inf])
+        KN.grouped_merge(dst, [dpt, dpv], torch.from_numpy(g).to(DEV), torch.from_numpy(sc).to(DEV),
+                         [torch.from_numpy(tok).to(DEV), torch.from_numpy(val).to(DEV)], K)
+    assert np.array_equal(dst.cpu().numpy(), st)
+    assert np.array_equal(dpt.cpu().numpy(), pt)
+    assert np.array_equal(dpv.cpu().numpy(), pv)
