@@ -17,6 +17,7 @@ Gram within the tolerances the reference's tests use).
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -107,6 +108,56 @@ def symmetrize_upper(U: np.ndarray) -> np.ndarray:
     """triu(U) + triu(U, 1)^T over the last two axes (core.py:756-759)."""
     up = np.triu(U)
     return up + np.swapaxes(np.triu(U, 1), -1, -2)
+
+
+# ----------------------------------------------------------------------------- host threads
+# numpy releases the GIL inside its array loops, so row / column chunks on a thread pool use every
+# host core; results are concatenated in order and equal the single-threaded expressions exactly.
+_POOL = None
+
+
+def _threads() -> int:
+    return max(1, int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1)))
+
+
+def _pool():
+    global _POOL
+    if _POOL is None:
+        from concurrent.futures import ThreadPoolExecutor
+        _POOL = ThreadPoolExecutor(max_workers=_threads())
+    return _POOL
+
+
+def _par_filter(H, valid, tp, ntn):
+    """nonzero(((H > tp) | (H < ntn)) & valid[:, None]) in row-major order, by row chunks."""
+    T = H.shape[0]
+    nt = _threads()
+    if nt == 1 or H.size < (1 << 22):
+        return np.nonzero(((H > tp[None, :]) | (H < ntn[None, :])) & valid[:, None])
+    bounds = np.linspace(0, T, nt + 1).astype(np.int64)
+
+    def part(i):
+        a, b = bounds[i], bounds[i + 1]
+        r, c = np.nonzero(((H[a:b] > tp[None, :]) | (H[a:b] < ntn[None, :])) & valid[a:b, None])
+        return r + a, c
+    res = list(_pool().map(part, range(nt)))
+    return np.concatenate([r for r, _ in res]), np.concatenate([c for _, c in res])
+
+
+def _par_ge(s, E):
+    """s[:, :, None] >= E[None] ([n, D, B] booleans) by column chunks."""
+    n, D = s.shape
+    nt = _threads()
+    if nt == 1 or s.size < (1 << 20):
+        return s[:, :, None] >= E[None]
+    out = np.empty((n, D, E.shape[-1]), bool)
+    bounds = np.linspace(0, D, nt + 1).astype(np.int64)
+
+    def part(i):
+        a, b = bounds[i], bounds[i + 1]
+        np.greater_equal(s[:, a:b, None], E[None, a:b], out=out[:, a:b])
+    list(_pool().map(part, range(nt)))
+    return out
 
 
 # ----------------------------------------------------------------------------- config / ctx
@@ -240,9 +291,7 @@ class AtlasOracle:
         if l in self._dense_layers:
             self._dense(l, H)
             return
-        valid = ctx.rowmap >= 0
-        mask = ((H > self.thr[l, 0][None, :]) | (H < -self.thr[l, 1][None, :])) & valid[:, None]
-        rr, cc = np.nonzero(mask)
+        rr, cc = _par_filter(H, ctx.rowmap >= 0, self.thr[l, 0], -self.thr[l, 1])
         cnt = rr.size
         vals = H[rr, cc].astype(np.float32)
         rows = ctx.rowmap[rr]
@@ -276,7 +325,7 @@ class AtlasOracle:
         levels = list(self.cfg.enrich_levels)
         for p, sgn in ((0, 1.0), (1, -1.0)):
             s = Hs * np.float32(sgn)
-            ge = s[:, :, None] >= self.E[l, p][None]
+            ge = _par_ge(s, self.E[l, p])
             cnt_ge = ge.sum(0)
             nxt = np.concatenate((cnt_ge[:, 1:], np.zeros_like(cnt_ge[:, :1])), 1)
             self.sub_bin[l, p] += cnt_ge - nxt
@@ -552,3 +601,41 @@ def offline_reference(Hs, toks, edges, K, Kr, rho_sub, seed=0, ann=None, levels=
     res = {k: np.stack(v) for k, v in out.items() if v}
     res["n_sub"] = int(sub.sum())
     return res
+
+
+# ----------------------------------------------------------------------------- pilot math
+def pilot_edges(Hs, probs=(0.5, 0.9, 0.99, 0.999, 0.9999)) -> np.ndarray:
+    """Quantile lower edges, strictly increasing along the bins (reference.py:55-75)."""
+    out = []
+    for H in Hs:
+        n, D = H.shape
+        idx = np.array([min(n - 1, int(round(q * (n - 1)))) for q in probs])
+        s = np.sort(np.asarray(H, np.float32), axis=0)
+        out.append(np.stack([s[idx].T, (-s[(n - 1) - idx]).T]))
+    E = np.stack(out).astype(np.float32)
+    for b in range(1, E.shape[-1]):
+        E[..., b] = np.maximum(E[..., b], np.nextafter(E[..., b - 1], np.float32(np.inf)))
+    return E
+
+
+def pilot_seeds(Hs, E, K, Kr, n_total, c=4.0, z=2.0):
+    """Seeds without protein groups (reference.py:78-122, groups=None branch)."""
+    tops, keys = [], []
+    for li, H in enumerate(Hs):
+        n, D = H.shape
+        kk = min(2 * K, n)
+        tp, kp = [], []
+        for p, sgn in ((0, 1.0), (1, -1.0)):
+            s = np.asarray(H, np.float32) * np.float32(sgn)
+            t = -np.partition(-s, kk - 1, axis=0)[kk - 1]
+            tp.append(nextdown(t))
+            ge = s[..., None] >= E[li, p][None]
+            in_bin = ge & ~np.concatenate((ge[..., 1:], np.zeros_like(ge[..., :1])), -1)
+            cnt = in_bin.sum(0).astype(np.float64)
+            m_lo = np.maximum(cnt - z * np.sqrt(cnt), 0) / n
+            with np.errstate(divide="ignore"):
+                theta = np.where(m_lo > 0, c * Kr * 2.0**32 / (n_total * m_lo), 2.0**32)
+            kp.append(np.floor(np.minimum(theta, 2.0**32)).astype(np.int64))
+        tops.append(np.stack(tp))
+        keys.append(np.stack(kp))
+    return np.stack(tops), np.stack(keys)

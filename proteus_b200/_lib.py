@@ -77,9 +77,23 @@ def load(path: str | os.PathLike | None = None):
     return lib
 
 
+# kernels launched per call (predicated kernels that exit early on the device still count)
+_KERNELS = {"atlas_grouped_merge": 6, "atlas_last_error": 0, "atlas_abi_version": 0}
+LAUNCHES = {"count": 0}
+
+
+def _n_kernels(name: str, args) -> int:
+    if name == "atlas_dense_select":
+        return 3 if args[14] else 1
+    if name.endswith("_bytes") or name.endswith("_i32"):
+        return 0
+    return _KERNELS.get(name, 1)
+
+
 def call(name: str, *args):
     """Call an entry point and raise AtlasKernelError on a non-zero status."""
     lib = load()
+    LAUNCHES["count"] += _n_kernels(name, args)
     rc = getattr(lib, name)(*args)
     if rc != 0:
         msg = lib.atlas_last_error().decode(errors="replace")

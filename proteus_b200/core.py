@@ -220,6 +220,7 @@ class Atlas:
         self._ws_top = KN.MergeWorkspace(dev)
         self._ws_res = KN.MergeWorkspace(dev)
         self._cap_cache = None
+        self.kernel_timer = None  # optional object with start(name) / stop(name) around kernel launches
 
     # ------------------------------------------------------------------ stats
     @property
@@ -353,10 +354,15 @@ class Atlas:
         cap = self._cap(ctx, l)
         st = stream_ptr(self.dev)
         dt = dtype_code(H.dtype)
+        kt = self.kernel_timer
         if not dense:
             cv, cr, cc = self._cand
+            if kt is not None:
+                kt.start("filter")
             call("atlas_filter_compact", ptr(H), dt, T, D, H.stride(0), ptr(ctx.rowmap32), ptr(self.thr[l, 0]),
                  ptr(self.thr[l, 1]), ptr(cv[l]), ptr(cr[l]), ptr(cc[l]), ptr(self._counts[l:l + 1]), cap, st)
+            if kt is not None:
+                kt.stop("filter")
         if self.cfg.subsample and l not in self._sub_done:
             self._subsample(l, H)
         if self.cfg.reservoir and not dense and ctx.n_r:
@@ -427,7 +433,12 @@ class Atlas:
     def _gram_layer(self, l: int):
         f = self._stage_fill[l]
         if f > 0:
+            kt = self.kernel_timer
+            if kt is not None:
+                kt.start("gram")
             KN.gram_upper(self._stage[l], f, self.gram[l])
+            if kt is not None:
+                kt.stop("gram", work=f)
             self._stage_fill[l] = 0
 
     def _drain_gram(self):

@@ -125,3 +125,13 @@ def test_oracle_merge_from_matches_reference():
     want = {k[2:]: v for k, v in z.items() if k.startswith("m_")}
     bad = compare(got, want)
     assert not bad, bad
+
+
+def test_oracle_pilot_math_matches_reference():
+    from tests.streams import pilot_inputs
+    Hs, _ = pilot_inputs()
+    z = golden("pilot")
+    E = O.pilot_edges(Hs)
+    assert np.array_equal(E, z["E"])
+    ts, rk = O.pilot_seeds(Hs, E, 16, 8, n_total=10**6)
+    assert np.array_equal(ts, z["top_seed_nogroups"]) and np.array_equal(rk, z["res_seed_key_nogroups"])
