@@ -32,6 +32,11 @@ enum atlas_status {
   ATLAS_ERR_UNSUPPORTED = 3
 };
 
+/* Device status word of the tensor-core kernels: 0, or the code of the first bounded wait that gave
+ * up (a kernel never hangs; it records the failure here and finishes). Synchronous read; `reset`
+ * clears it. No counterpart in the reference (its Triton kernels have no waits). */
+int atlas_device_status(int* status_host, int reset);
+
 /* Message of the last error raised on the calling host thread ("" if none). */
 const char* atlas_last_error(void);
 /* ABI version of this library (bumped on any signature change). */
@@ -104,7 +109,8 @@ int atlas_count_gemm_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int
  * Upper-block-triangle Gram on tcgen05 tensor cores — replaces gram_accumulate
  * (atlas/stats_triton.py:234-255): C[D, D] (fp32, row-major, contiguous) += X^T X on the 128x128
  * blocks with block row <= block column; lower blocks untouched. X is supplied transposed:
- * XT [D, n] bf16 or fp16 with leading dimension ldx (elements; ldx % 8 == 0, 16-byte aligned base).
+ * XT [D, n] bf16 or fp16 (tcgen05, fp32 accumulation) or fp32 (exact fp32 FMA on CUDA cores) with
+ * leading dimension ldx (elements; ldx % 8 == 0, 16-byte aligned base).
  */
 int atlas_gram_upper(const void* XT, int dtype, int64_t ldx, int64_t n, int64_t D, float* C, void* stream);
 

@@ -3,57 +3,57 @@
 // Replaces filter_candidates (atlas/filter_triton.py:19-86). B200 layout: each warp owns a strip of
 // 32 * VEC consecutive columns (one 16-byte vector per lane, VEC = 8 for bf16/fp16, 4 for fp32) and
 // walks rows with U rows in flight per lane; the per-column thresholds live in registers for the
-// whole walk. Padding rows (rowmap < 0) are never read. Survivors are compacted with a warp ballot
-// + shuffle prefix sum and ONE global atomic per warp per U-row step that has any hit; survivors
-// are rare (~0.1-0.5% of elements), so almost every step takes the ballot fast path.
+// whole walk. Padding rows (rowmap < 0) are never read.
+// Compaction is two-level: a warp ballot + shuffle prefix sum places a step's survivors in a
+// per-CTA staging area in shared memory (one shared-memory atomic per warp step with hits), and
+// the CTA reserves its global output range with ONE global atomic at the end, then copies the
+// staged survivors out with coalesced stores. At ~0.1-0.5% survivors nearly every warp step has a
+// hit, so per-step global atomics on the single counter would serialise the whole pass; a warp
+// whose step does not fit the staging area writes directly (global atomic), which keeps the
+// count exact for any survivor density.
 #include "common.cuh"
 
 namespace atlas {
 namespace {
 
+// Raw vector of VEC elements as loaded (16 bytes on the vector paths); elements are widened to
+// fp32 on use, so a lane keeps U raw vectors in flight in few registers.
 template <int DT, int VEC>
-struct VecLoad;
+struct Vec;
 
 template <>
-struct VecLoad<ATLAS_BF16, 8> {
-  static __device__ __forceinline__ void load(const void* p, float (&x)[8]) {
-    uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      x[2 * k] = __uint_as_float(w[k] << 16);
-      x[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
-    }
+struct Vec<ATLAS_BF16, 8> {
+  uint4 v;
+  __device__ __forceinline__ void load(const void* p) { v = __ldcs(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ float at(int k) const {
+    const uint32_t w = k < 2 ? v.x : k < 4 ? v.y : k < 6 ? v.z : v.w;
+    return (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
   }
 };
 template <>
-struct VecLoad<ATLAS_F16, 8> {
-  static __device__ __forceinline__ void load(const void* p, float (&x)[8]) {
-    uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
-    const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float2 f = __half22float2(h[k]);
-      x[2 * k] = f.x;
-      x[2 * k + 1] = f.y;
-    }
+struct Vec<ATLAS_F16, 8> {
+  uint4 v;
+  __device__ __forceinline__ void load(const void* p) { v = __ldcs(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ float at(int k) const {
+    const uint32_t w = k < 2 ? v.x : k < 4 ? v.y : k < 6 ? v.z : v.w;
+    return __half2float(__ushort_as_half((unsigned short)((k & 1) ? (w >> 16) : (w & 0xFFFFu))));
   }
 };
 template <>
-struct VecLoad<ATLAS_F32, 4> {
-  static __device__ __forceinline__ void load(const void* p, float (&x)[4]) {
-    float4 v = __ldcs(reinterpret_cast<const float4*>(p));
-    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
-  }
+struct Vec<ATLAS_F32, 4> {
+  float4 v;
+  __device__ __forceinline__ void load(const void* p) { v = __ldcs(reinterpret_cast<const float4*>(p)); }
+  __device__ __forceinline__ float at(int k) const { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
 };
 template <int DT>
-struct VecLoad<DT, 1> {
-  static __device__ __forceinline__ void load(const void* p, float (&x)[1]) {
-    x[0] = Elem<DT>::f(*reinterpret_cast<const typename Elem<DT>::T*>(p));
-  }
+struct Vec<DT, 1> {
+  float v;
+  __device__ __forceinline__ void load(const void* p) { v = Elem<DT>::f(*reinterpret_cast<const typename Elem<DT>::T*>(p)); }
+  __device__ __forceinline__ float at(int) const { return v; }
 };
 
 constexpr int kWarps = 8;
+constexpr int kStage = 2048;  // staged survivors per CTA (24 KB of shared memory)
 
 template <int DT, int VEC, int U>
 __global__ void __launch_bounds__(kWarps * 32)
@@ -73,31 +73,36 @@ filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes
     tp[k] = ok ? __ldg(thr_pos + c0 + k) : __int_as_float(0x7F800000);    // +inf: never survives
     tn[k] = ok ? -__ldg(thr_neg + c0 + k) : __int_as_float(0xFF800000);   // h < -thr_neg
   }
+  __shared__ float s_val[kStage];
+  __shared__ int32_t s_row[kStage], s_col[kStage];
+  __shared__ int s_n, s_limit, s_base;
+  if (threadIdx.x == 0) {
+    s_n = 0;
+    s_limit = kStage;
+  }
+  __syncthreads();
   const int64_t r_begin = (int64_t)blockIdx.y * rows_per_cta;
   int64_t r_end = r_begin + rows_per_cta;
   if (r_end > T) r_end = T;
 
   for (int64_t r = r_begin + warp; r < r_end; r += (int64_t)kWarps * U) {
-    float x[U][VEC];
+    Vec<DT, VEC> x[U];
     int32_t vr[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t row = r + (int64_t)u * kWarps;
       vr[u] = row < r_end ? __ldg(rowmap + row) : -1;
-      if (vr[u] >= 0 && col_ok) {
-        VecLoad<DT, VEC>::load(H + row * ld_bytes + c0 * (int64_t)sizeof(E), x[u]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) x[u][k] = 0.0f;
-        vr[u] = -1;
-      }
+      if (!col_ok) vr[u] = -1;
+      if (vr[u] >= 0) x[u].load(H + row * ld_bytes + c0 * (int64_t)sizeof(E));
     }
     uint32_t bits = 0;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
+      if (vr[u] < 0) continue;
 #pragma unroll
       for (int k = 0; k < VEC; ++k) {
-        const bool hit = (vr[u] >= 0) && ((x[u][k] > tp[k]) || (x[u][k] < tn[k]));
+        const float h = x[u].at(k);
+        const bool hit = (h > tp[k]) || (h < tn[k]);
         bits |= (hit ? 1u : 0u) << (u * VEC + k);
       }
     }
@@ -106,22 +111,47 @@ filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes
     const int n = __popc(bits);
     const int pre = warp_excl_scan(n, lane, &total);
     int base = 0;
-    if (lane == 31) base = atomicAdd(count, total);
+    if (lane == 31) base = atomicAdd(&s_n, total);
     base = __shfl_sync(0xFFFFFFFFu, base, 31);
+    const bool staged = base + total <= kStage;
+    if (!staged) {  // staging area full: this step goes straight to global memory
+      if (lane == 31) {
+        atomicMin(&s_limit, base);  // reservations grow monotonically: the first miss ends the staged prefix
+        base = atomicAdd(count, total);
+      }
+      base = __shfl_sync(0xFFFFFFFFu, base, 31);
+    }
     int64_t slot = (int64_t)base + pre;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
 #pragma unroll
       for (int k = 0; k < VEC; ++k) {
         if (bits & (1u << (u * VEC + k))) {
-          if (slot < cap) {
-            out_val[slot] = x[u][k];
+          if (staged) {
+            s_val[slot] = x[u].at(k);
+            s_row[slot] = vr[u];
+            s_col[slot] = (int32_t)(c0 + k);
+          } else if (slot < cap) {
+            out_val[slot] = x[u].at(k);
             out_row[slot] = vr[u];
             out_col[slot] = (int32_t)(c0 + k);
           }
           ++slot;
         }
       }
+    }
+  }
+  __syncthreads();
+  const int staged_n = s_n < s_limit ? s_n : s_limit;  // [0, staged_n) holds every staged survivor
+  if (threadIdx.x == 0) s_base = staged_n > 0 ? atomicAdd(count, staged_n) : 0;
+  __syncthreads();
+  const int64_t base = s_base;
+  for (int i = threadIdx.x; i < staged_n; i += blockDim.x) {
+    const int64_t slot = base + i;
+    if (slot < cap) {
+      out_val[slot] = s_val[i];
+      out_row[slot] = s_row[i];
+      out_col[slot] = s_col[i];
     }
   }
 }

@@ -1,0 +1,359 @@
+// Tensor-core contractions on tcgen05 / TMEM (sm_100a), TMA-fed, warp-specialised:
+//   warp 0: TMA producer (one elected lane), warp 1: MMA issuer (one lane; owns the TMEM
+//   allocation), warps 2-5: epilogue (TMEM -> registers -> global), one thread per accumulator row.
+//
+// atlas_gram_upper  C[D, D] += X^T X on the upper 128-block triangle (gram_accumulate,
+//                   stats_triton.py:234-255). One CTA per 128x128 output block; bf16/fp16 operands
+//                   from the transposed staging XT [D, n] (both operands K-major, 128-byte swizzle);
+//                   fp32 accumulation in TMEM in segments of 1024 rows, double-buffered so the
+//                   epilogue folds a finished segment into register totals while the next one is
+//                   computed (two-level fp32 summation: error of a 1024-row sum, not an n-row one);
+//                   diagonal blocks load their single operand once. C is read and written once.
+// atlas_count_gemm_i8  out[M, A] += masks[M, n_pad] . annT[A_pad, n_pad]^T, exact (kind::i8,
+//                   int32 accumulate, int64 output), one CTA per 128 mask rows.
+//
+// Every wait is bounded: a wait that gives up records a code in the device status word
+// (atlas_device_status) and the kernel finishes without further work.
+#include <cuda.h>
+
+#include "tc.cuh"
+
+namespace atlas {
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int esize, uint64_t inner,
+                 uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swz) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                              const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return fail(ATLAS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    encode = reinterpret_cast<Encode>(fn);
+  }
+  (void)esize;
+  if ((uintptr_t)base % 16 != 0 || row_stride_bytes % 16 != 0)
+    return fail(ATLAS_ERR_ARG, "tensor map: base and row stride must be 16-byte aligned");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ATLAS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return ATLAS_OK;
+}
+
+namespace {
+using namespace tc;
+
+constexpr int kThreads = 192;
+
+// ------------------------------------------------------------------------------------------ Gram
+constexpr int GB = 128;               // output block (M = N = 128)
+constexpr int GK = 64;                // bf16 elements per K chunk (128 bytes)
+constexpr int G_STAGES = 6;
+constexpr int G_SEG = 16;             // K chunks per TMEM segment (1024 rows)
+constexpr uint32_t G_TILE = GB * GK * 2;  // 16 KB
+
+struct GramSmem {
+  uint8_t a[G_STAGES][G_TILE];
+  uint8_t b[G_STAGES][G_TILE];
+  uint64_t full[G_STAGES], empty[G_STAGES], tfull[2], tempty[2];
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+gram_tc_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t D, int nb, float* __restrict__ C,
+               uint32_t idesc) {
+  extern __shared__ uint8_t gram_raw[];
+  GramSmem& s = *reinterpret_cast<GramSmem*>((reinterpret_cast<uintptr_t>(gram_raw) + 1023) & ~uintptr_t(1023));
+  int t = blockIdx.x, bi = 0;
+  while (t >= nb - bi) {
+    t -= nb - bi;
+    ++bi;
+  }
+  const int bj = bi + t;
+  const bool diag = bi == bj;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (int)((n + GK - 1) / GK);
+  const int nseg = (nk + G_SEG - 1) / G_SEG;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < G_STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&s.tmem_base, 256);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmap);
+      const uint32_t bytes = diag ? G_TILE : 2 * G_TILE;
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % G_STAGES;
+        const uint32_t ph = (k / G_STAGES) & 1;
+        if (k >= G_STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 101)) break;
+        mbar_arrive_expect_tx(&s.full[st], bytes);
+        tma_load_2d(s.a[st], &tmap, k * GK, bi * GB, &s.full[st]);
+        if (!diag) tma_load_2d(s.b[st], &tmap, k * GK, bj * GB, &s.full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % G_STAGES;
+        const uint32_t ph = (k / G_STAGES) & 1;
+        const int seg = k / G_SEG, buf = seg & 1;
+        const bool first = (k % G_SEG) == 0;
+        if (first && seg >= 2 && !mbar_wait(&s.tempty[buf], ((seg >> 1) - 1) & 1, 102)) break;
+        if (!mbar_wait(&s.full[st], ph, 103)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(s.a[st]);
+        const uint32_t b_addr = diag ? a_addr : smem_u32(s.b[st]);
+#pragma unroll
+        for (int kk = 0; kk < GK / 16; ++kk)
+          mma_f16(tmem + buf * GB, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                  (first && kk == 0) ? 0u : 1u);
+        mma_commit(&s.empty[st]);
+        if ((k % G_SEG) == G_SEG - 1 || k == nk - 1) mma_commit(&s.tfull[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to warps with warp % 4 == q
+    const int row = q * 32 + lane;
+    float tot[GB];
+#pragma unroll
+    for (int c = 0; c < GB; ++c) tot[c] = 0.f;
+    bool ok = true;
+    for (int seg = 0; seg < nseg; ++seg) {
+      const int buf = seg & 1;
+      if (!mbar_wait(&s.tfull[buf], (seg >> 1) & 1, 104)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < GB / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * GB + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tot[c * 32 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s.tempty[buf]);
+    }
+    const int64_t gi = (int64_t)bi * GB + row;
+    if (ok && gi < D) {
+      float* crow = C + gi * D + (int64_t)bj * GB;
+      const int64_t jmax = D - (int64_t)bj * GB;
+      const bool vec = (D % 4 == 0) && jmax >= GB;
+      if (vec) {
+#pragma unroll
+        for (int c = 0; c < GB; c += 4) {
+          float4 v = *reinterpret_cast<float4*>(crow + c);
+          v.x += tot[c]; v.y += tot[c + 1]; v.z += tot[c + 2]; v.w += tot[c + 3];
+          *reinterpret_cast<float4*>(crow + c) = v;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < GB; ++c)
+          if (c < jmax) crow[c] += tot[c];
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------------------------------ int8
+constexpr int IM = 128;               // mask rows per CTA
+constexpr int IK = 128;               // int8 K chunk (128 bytes)
+constexpr int I_STAGES = 4;
+
+template <int AP>
+struct I8Smem {
+  uint8_t a[I_STAGES][IM * IK];
+  uint8_t b[I_STAGES][AP * IK];
+  uint64_t full[I_STAGES], empty[I_STAGES], tfull;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+template <int AP>
+__global__ void __launch_bounds__(kThreads, 1)
+count_i8_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, int64_t M,
+                   int64_t n_pad, int64_t* __restrict__ out, int64_t A, uint32_t tcols) {
+  extern __shared__ uint8_t i8_raw[];
+  I8Smem<AP>& s = *reinterpret_cast<I8Smem<AP>*>((reinterpret_cast<uintptr_t>(i8_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.x * IM;
+  const int nk = (int)(n_pad / IK);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < I_STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    mbar_init(&s.tfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&s.tmem_base, tcols);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  constexpr uint32_t idesc = idesc_s8_s32(IM, AP);
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tm_a);
+      prefetch_tmap(&tm_b);
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % I_STAGES;
+        const uint32_t ph = (k / I_STAGES) & 1;
+        if (k >= I_STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 201)) break;
+        mbar_arrive_expect_tx(&s.full[st], IM * IK + AP * IK);
+        tma_load_2d(s.a[st], &tm_a, k * IK, (int32_t)m0, &s.full[st]);
+        tma_load_2d(s.b[st], &tm_b, k * IK, 0, &s.full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % I_STAGES;
+        const uint32_t ph = (k / I_STAGES) & 1;
+        if (!mbar_wait(&s.full[st], ph, 202)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(s.a[st]), b_addr = smem_u32(s.b[st]);
+#pragma unroll
+        for (int kk = 0; kk < IK / 32; ++kk)
+          mma_i8(tmem, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                 (k == 0 && kk == 0) ? 0u : 1u);
+        mma_commit(&s.empty[st]);
+      }
+      mma_commit(&s.tfull);
+    }
+  } else {
+    const int q = warp & 3;
+    const int64_t m = m0 + q * 32 + lane;
+    if (mbar_wait(&s.tfull, 0, 203)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < AP; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c, r);
+        tmem_ld_wait();
+        if (m < M) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c + j < A) out[m * A + c + j] += (int64_t)(int32_t)r[j];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, tcols);
+}
+
+template <int AP>
+int launch_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int8_t* annT, int64_t* out, int64_t A,
+              cudaStream_t st) {
+  CUtensorMap ta, tb;
+  if (int e = make_tmap_2d(&ta, masks, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n_pad, M, n_pad, IK, IM,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  if (int e = make_tmap_2d(&tb, annT, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n_pad, AP, n_pad, IK, AP,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  const size_t smem = sizeof(I8Smem<AP>) + 1024;
+  if (cudaFuncSetAttribute(count_i8_tc_kernel<AP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return fail(ATLAS_ERR_CUDA, "count_gemm_i8: cannot reserve %zu bytes of shared memory", smem);
+  uint32_t tcols = 32;
+  while (tcols < (uint32_t)AP) tcols <<= 1;
+  count_i8_tc_kernel<AP><<<(unsigned)((M + IM - 1) / IM), kThreads, smem, st>>>(ta, tb, M, n_pad, out, A, tcols);
+  return check_launch("atlas_count_gemm_i8");
+}
+
+}  // namespace
+
+// fp32 activations keep an exact-FMA CUDA-core Gram (tcgen05 has no IEEE fp32 operand kind)
+int gram_upper_f32(const float* XT, int64_t ldx, int64_t n, int64_t D, float* C, cudaStream_t st);
+
+}  // namespace atlas
+
+using namespace atlas;
+
+extern "C" int atlas_device_status(int* status_host, int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tc::g_device_status, sizeof(int)) != cudaSuccess)
+    return fail(ATLAS_ERR_CUDA, "device_status: read failed");
+  if (status_host) *status_host = v;
+  if (reset && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(tc::g_device_status, &z, sizeof(int)) != cudaSuccess)
+      return fail(ATLAS_ERR_CUDA, "device_status: reset failed");
+  }
+  return ATLAS_OK;
+}
+
+extern "C" int atlas_gram_upper(const void* XT, int dtype, int64_t ldx, int64_t n, int64_t D, float* C, void* stream) {
+  ATLAS_REQUIRE(n >= 0 && D >= 0 && ldx >= n, "gram_upper: bad sizes");
+  if (n == 0 || D == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(XT && C, "gram_upper: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == ATLAS_F32) return gram_upper_f32((const float*)XT, ldx, n, D, C, st);
+  ATLAS_REQUIRE(dtype == ATLAS_BF16 || dtype == ATLAS_F16, "gram_upper: unknown dtype %d", dtype);
+  ATLAS_REQUIRE(ldx % 8 == 0 && (uintptr_t)XT % 16 == 0, "gram_upper: XT must be 16-byte aligned with ldx %% 8 == 0");
+  ATLAS_REQUIRE(D < (1LL << 31) && n < (1LL << 31), "gram_upper: sizes exceed int32 coordinates");
+  CUtensorMap tm;
+  if (int e = make_tmap_2d(&tm, XT, dtype == ATLAS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           2, (uint64_t)n, (uint64_t)D, (uint64_t)ldx * 2, GK, GB, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  const int nb = (int)((D + GB - 1) / GB);
+  const int64_t tiles = (int64_t)nb * (nb + 1) / 2;
+  const size_t smem = sizeof(GramSmem) + 1024;
+  if (cudaFuncSetAttribute(gram_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return fail(ATLAS_ERR_CUDA, "gram_upper: cannot reserve %zu bytes of shared memory", smem);
+  const uint32_t idesc = dtype == ATLAS_BF16 ? tc::idesc_bf16_f32(GB, GB) : tc::idesc_f16_f32(GB, GB);
+  gram_tc_kernel<<<(unsigned)tiles, kThreads, smem, st>>>(tm, n, D, nb, C, idesc);
+  return check_launch("atlas_gram_upper");
+}
+
+extern "C" int atlas_count_gemm_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int8_t* annT, int64_t A_pad,
+                                   int64_t* out, int64_t A, void* stream) {
+  ATLAS_REQUIRE(M >= 0 && n_pad >= 0 && n_pad % IK == 0, "count_gemm_i8: n_pad must be a multiple of %d", IK);
+  ATLAS_REQUIRE(A_pad % 16 == 0 && A_pad >= 16 && A_pad <= 256 && A >= 0 && A <= A_pad, "count_gemm_i8: bad A/A_pad");
+  if (M == 0 || n_pad == 0 || A == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(masks && annT && out, "count_gemm_i8: null pointer");
+  ATLAS_REQUIRE((uintptr_t)masks % 16 == 0 && (uintptr_t)annT % 16 == 0, "count_gemm_i8: operands must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (A_pad) {
+    case 16: return launch_i8<16>(masks, M, n_pad, annT, out, A, st);
+    case 32: return launch_i8<32>(masks, M, n_pad, annT, out, A, st);
+    case 48: return launch_i8<48>(masks, M, n_pad, annT, out, A, st);
+    case 64: return launch_i8<64>(masks, M, n_pad, annT, out, A, st);
+    case 96: return launch_i8<96>(masks, M, n_pad, annT, out, A, st);
+    case 128: return launch_i8<128>(masks, M, n_pad, annT, out, A, st);
+    case 256: return launch_i8<256>(masks, M, n_pad, annT, out, A, st);
+    default: return fail(ATLAS_ERR_UNSUPPORTED, "count_gemm_i8: A_pad %lld not instantiated", (long long)A_pad);
+  }
+}

@@ -167,3 +167,13 @@ def test_grouped_merge_large_random_vs_oracle():
     assert np.array_equal(dst.cpu().numpy(), st)
     assert np.array_equal(dpt.cpu().numpy(), pt)
     assert np.array_equal(dpv.cpu().numpy(), pv)
+
+
+def test_device_status_clean_after_tensor_core_kernels():
+    """No bounded wait of the tcgen05 kernels gave up during this session."""
+    import ctypes
+    from proteus_b200 import _lib
+    torch.cuda.synchronize()
+    st = ctypes.c_int(-1)
+    assert _lib.load().atlas_device_status(ctypes.byref(st), 0) == 0
+    assert st.value == 0
