@@ -1,0 +1,119 @@
+"""Data-parallel atlas over the GPUs of one node: one process per GPU, disjoint sequence shards,
+an exact combine of the shard states at the end.
+
+The stream shards with no communication: every rank runs the full forward + atlas on the batches
+`plan[rank::world]`, with edges and seeds computed from the GLOBAL stream (the reference's merge
+contract, tests/test_resume_merge.py:56-60; Atlas.merge_from asserts it, atlas/core.py:632-634).
+
+`merge_states` is merge_from (atlas/core.py:628-654) across ranks:
+  top-K / reservoirs: the G group rows are cut into `world` slices; an all-to-all sends slice r of
+    every rank to rank r, which merges the `world` sorted copies of its slice (the GPU row merge:
+    keys are unique across shards, so the result is the exact top-K / bottom-Kr of the union) and
+    an all-gather returns the merged rows to every rank (each row crosses NVLink twice, instead of
+    every rank receiving every rank's whole state);
+  counts (sub_bin, enr, ann_tot, n_seen, n_sub): all-reduce SUM in int64 (exact);
+  moments (sub_sum, sub_sq, fp64): all-gathered and summed in rank order (deterministic);
+  Gram: each rank flushes to fp64 and the fp64 matrices are summed in rank order, layer by layer.
+"""
+from __future__ import annotations
+
+import zlib
+
+import torch
+import torch.distributed as dist
+
+I64_MIN = torch.iinfo(torch.int64).min
+
+
+def shard_plan(plan: list, world: int, rank: int) -> list:
+    """Batches of this rank: plan[rank::world] (disjoint, covering, deterministic)."""
+    return plan[rank::world]
+
+
+def _row_merge_cuda(sc, tok, val, osc, otok, oval):
+    from .kernels import merge_rows
+    merge_rows(sc, tok, val, osc, otok, oval)
+
+
+def _exchange_rows(sc, tok, val, fills, world, group, row_merge):
+    """All-to-all of row slices, merge of the `world` copies, all-gather of the merged slices."""
+    G, K = sc.shape
+    per = -(-G // world)
+    Gp = per * world
+    dev = sc.device
+
+    def pad(t, fill):
+        if Gp == G:
+            return t.contiguous()
+        p = torch.full((Gp - G, K), fill, dtype=t.dtype, device=dev)
+        return torch.cat([t, p]).contiguous()
+
+    parts = [pad(sc, I64_MIN), pad(tok, fills[0]), pad(val, fills[1])]
+    recv = [torch.empty_like(p) for p in parts]
+    for src, dst in zip(parts, recv):
+        dist.all_to_all_single(dst, src, group=group)
+    # recv[i] holds, for every source rank s, rows [s*per, (s+1)*per) = this rank's slice from rank s
+    mine = [r.view(world, per, K) for r in recv]
+    acc = [mine[i][0].clone() for i in range(3)]
+    for s in range(1, world):
+        row_merge(acc[0], acc[1], acc[2], mine[0][s].contiguous(), mine[1][s].contiguous(), mine[2][s].contiguous())
+    out = [torch.empty_like(p) for p in parts]
+    for o, a in zip(out, acc):
+        dist.all_gather_into_tensor(o, a.contiguous(), group=group)
+    return [o[:G] for o in out]
+
+
+def _sum_in_rank_order(t: torch.Tensor, world, group) -> torch.Tensor:
+    bufs = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(bufs, t.contiguous(), group=group)
+    acc = bufs[0].clone()
+    for b in bufs[1:]:
+        acc += b
+    return acc
+
+
+@torch.no_grad()
+def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
+    """Combine the shard atlases of all ranks in place; afterwards every rank holds the merged
+    atlas (equal to merge_from applied over all shards). `atlas` needs the reference's state
+    attributes (top_k/top_t/top_s, res_s/res_t/res_v, sub_*, enr/ann_tot, n_seen/n_sub, stats,
+    E, top_seed, res_seed, cfg). `row_merge` defaults to the GPU row merge (atlas_merge_rows)."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return atlas
+    row_merge = row_merge or _row_merge_cuda
+    # the shards must share edges, config and both seeds (atlas/core.py:632-634)
+    sig = torch.tensor([float(atlas.E.double().sum()), float(atlas.top_seed.double().nan_to_num(0, 0, 0).sum()),
+                        float(atlas.res_seed.double().sum()), float(zlib.crc32(repr(sorted(atlas.cfg.__dict__.items())).encode()))],
+                       dtype=torch.float64, device=atlas.top_k.device)
+    sigs = [torch.empty_like(sig) for _ in range(world)]
+    dist.all_gather(sigs, sig, group=group)
+    if not all(torch.equal(sigs[0], s) for s in sigs[1:]):
+        raise ValueError("shards must share edges, config and seeds (derive them from the GLOBAL stream)")
+    atlas.top_k, atlas.top_t, atlas.top_s = _exchange_rows(atlas.top_k, atlas.top_t, atlas.top_s, (-1, float("-inf")),
+                                                           world, group, row_merge)
+    atlas.res_s, atlas.res_t, atlas.res_v = _exchange_rows(atlas.res_s, atlas.res_t, atlas.res_v, (-1, float("nan")),
+                                                           world, group, row_merge)
+    for k in ("sub_bin",) + (("enr", "ann_tot") if getattr(atlas, "n_a", 0) else ()):
+        t = getattr(atlas, k)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    for k in ("sub_sum", "sub_sq"):
+        getattr(atlas, k).copy_(_sum_in_rank_order(getattr(atlas, k), world, group))
+    dev = atlas.top_k.device
+    cnt = torch.tensor([atlas.n_seen, atlas.n_sub, getattr(atlas, "gram_rows", 0)], dtype=torch.int64, device=dev)
+    dist.all_reduce(cnt, op=dist.ReduceOp.SUM, group=group)
+    atlas.n_seen, atlas.n_sub = int(cnt[0]), int(cnt[1])
+    if gram and getattr(atlas, "gram", None) is not None:
+        atlas.flush_gram()
+        for l in range(atlas.gram64.shape[0]):
+            g = atlas.gram64[l].to(dev)
+            atlas.gram64[l].copy_(_sum_in_rank_order(g, world, group).cpu())
+        atlas.gram_rows = int(cnt[2])
+    stats = [None] * world
+    dist.all_gather_object(stats, dict(atlas.stats), group=group)
+    merged = {}
+    for st in stats:
+        for k, v in st.items():
+            merged[k] = merged.get(k, 0) + v
+    atlas.stats = merged
+    return atlas

@@ -1,0 +1,333 @@
+"""End-to-end atlas run, resumable — drop-in for haelyons/proteus scripts/run_atlas.py (same flags).
+
+  python -m proteus_b200.run_atlas --model 650M --data data.pt --out runs/x [--resume] ...
+  torchrun --nproc-per-node 8 -m proteus_b200.run_atlas ...   (one shard of the batch plan per GPU)
+
+Outputs in --out (as the reference, run_atlas.py:3-8): ckpt/ckpt_<batch>.pt (atomic, last 2 kept),
+batches.jsonl (one record per batch), run.json (summary), atlas.pt (final result + sha256 digests of
+the exact fields). With several ranks each rank checkpoints its own shard under ckpt/rank<r>/ and
+the shard states are combined exactly (proteus_b200.dist.merge_states) before rank 0 writes atlas.pt.
+
+--data accepts the reference's Swiss-Prot .pt format or `synthetic:<n_seq>[:<seed>]` (C4-like
+synthetic proteins). Models are built from their published architecture with a seeded random init
+(no network), or loaded from a local HuggingFace directory.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import queue
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+from .core import Atlas, AtlasConfig
+from .data import SwissProt, shuffled_order, synthetic_dataset
+from .esm import attach, flops_per_batch, load, pilot
+from .pilot import pilot_edges, pilot_seeds
+
+
+def sync(dev):
+    if torch.device(dev).type == "cuda":
+        torch.cuda.synchronize()
+
+
+def atomic_save(obj, path: Path):
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    torch.save(obj, tmp)
+    with open(tmp, "rb") as f:
+        os.fsync(f.fileno())
+    os.replace(tmp, path)
+
+
+def latest_ckpt(d: Path):
+    c = sorted(d.glob("ckpt_*.pt"), key=lambda p: int(p.stem.split("_")[1]))
+    return c[-1] if c else None
+
+
+def parser():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="8M")
+    ap.add_argument("--control", default="none", choices=["none", "shuffled", "random"])
+    ap.add_argument("--control-seed", type=int, default=None)
+    ap.add_argument("--data", required=True)
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--device", default="cuda")
+    ap.add_argument("--dtype", default="bf16")
+    ap.add_argument("--max-seqs", type=int, default=0)
+    ap.add_argument("--tokens-per-batch", type=int, default=32768)
+    ap.add_argument("--window", type=int, default=8192)
+    ap.add_argument("--sorted-batches", action="store_true")
+    ap.add_argument("--pilot-tokens", type=int, default=32768)
+    ap.add_argument("--K", type=int, default=64)
+    ap.add_argument("--Kr", type=int, default=16)
+    ap.add_argument("--backend", default="torch")
+    ap.add_argument("--cap-frac-early", type=float, default=0.0)
+    ap.add_argument("--stats-impl", default="v3", choices=["v3", "v2", "v1"])
+    ap.add_argument("--merge-impl", default="stacked", choices=["stacked", "loop"])
+    ap.add_argument("--no-reservoir", action="store_true")
+    ap.add_argument("--no-subsample", action="store_true")
+    ap.add_argument("--no-gram", action="store_true")
+    ap.add_argument("--naive", action="store_true")
+    ap.add_argument("--count-ties", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--ckpt-every", type=int, default=500)
+    ap.add_argument("--gram-flush-every", type=int, default=500)
+    ap.add_argument("--resume", action="store_true")
+    ap.add_argument("--stop-after", type=int, default=0)
+    ap.add_argument("--seed-thresholds", action="store_true")
+    ap.add_argument("--pair-forward", action="store_true")
+    ap.add_argument("--pair-every", type=int, default=0)
+    ap.add_argument("--plan-offset", type=int, default=0)
+    ap.add_argument("--prefetch", type=int, default=2)
+    ap.add_argument("--only-acc", default=None)
+    ap.add_argument("--edges-from", default=None)
+    ap.add_argument("--exclude-acc", default=None)
+    ap.add_argument("--edge-q", type=float, nargs="+", default=[0.5, 0.9, 0.99, 0.999, 0.9999])
+    ap.add_argument("--profile-at", type=int, nargs="*", default=[])
+    ap.add_argument("--max-batches", type=int, default=0)
+    ap.add_argument("--deadline", type=float, default=0.0)
+    return ap
+
+
+def _args_key(a) -> dict:
+    keep = ["model", "control", "data", "dtype", "max_seqs", "tokens_per_batch", "window", "sorted_batches",
+            "pilot_tokens", "K", "Kr", "no_reservoir", "no_subsample", "no_gram", "naive", "seed",
+            "seed_thresholds", "max_batches", "exclude_acc", "edge_q", "only_acc", "edges_from"]
+    key = {k: getattr(a, k) for k in keep}
+    if getattr(a, "control_seed", None) is not None:
+        key["control_seed"] = a.control_seed
+    return key
+
+
+def _dataset(spec: str):
+    if spec.startswith("synthetic:"):
+        parts = spec.split(":")
+        return SwissProt(synthetic_dataset(int(parts[1]), seed=int(parts[2]) if len(parts) > 2 else 0))
+    return SwissProt(spec)
+
+
+def _prefetch(it, n):
+    q, end = queue.Queue(maxsize=n), object()
+
+    def work():
+        try:
+            for x in it:
+                q.put(x)
+        except BaseException as e:  # noqa: BLE001
+            q.put(e)
+        q.put(end)
+    threading.Thread(target=work, daemon=True).start()
+    while True:
+        x = q.get()
+        if x is end:
+            return
+        if isinstance(x, BaseException):
+            raise x
+        yield x
+
+
+def main(argv=None):
+    a = parser().parse_args(argv)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800),
+                                             device_id=torch.device("cuda", local))
+        dev = f"cuda:{local}"
+    else:
+        dev = a.device
+    out = Path(a.out)
+    ck_dir = out / "ckpt" if world == 1 else out / "ckpt" / f"rank{rank}"
+    ck_dir.mkdir(parents=True, exist_ok=True)
+    dtype = {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[a.dtype]
+    log = (lambda *x: print(*x, flush=True)) if rank == 0 else (lambda *x: None)
+
+    t0 = time.time()
+    ds = _dataset(a.data)
+    order = shuffled_order(len(ds), a.seed)
+    n_excluded = 0
+
+    def acc_set(path):
+        return {ln.split("\t")[0].split(",")[0].strip() for ln in open(path) if ln.strip() and not ln.startswith("Entry")}
+    if a.only_acc:
+        inc = acc_set(a.only_acc)
+        order = order[torch.tensor([ds.d["acc"][i] in inc for i in order.tolist()], dtype=torch.bool)]
+    if a.exclude_acc:
+        ex = acc_set(a.exclude_acc)
+        drop = torch.tensor([acc in ex for acc in ds.d["acc"]], dtype=torch.bool)
+        keep = ~drop[order]
+        n_excluded = int((~keep).sum())
+        order = order[keep]
+    if a.max_seqs:
+        order = order[: a.max_seqs]
+    ctl_seed = a.seed if a.control_seed is None else a.control_seed
+    model, tok, info = load(a.model, a.control, dtype=dtype, device=dev, seed=ctl_seed)
+    info["control_seed"] = ctl_seed
+    vocab = tok.get_vocab()
+    L, D = info["n_layers"], info["d_ff"]
+    plan = ds.plan(order, a.tokens_per_batch, a.window, a.seed, shuffle_batches=not a.sorted_batches)
+    if a.max_batches:
+        plan = plan[: a.max_batches]
+    n_total = int(sum(min(int(ds.len[i]), ds.max_res) for grp in plan for i in grp))
+    t_load = time.time() - t0
+
+    cfg = AtlasConfig(K=a.K, Kr=a.Kr, backend=a.backend, seed=a.seed, reservoir=not a.no_reservoir,
+                      subsample=not a.no_subsample, gram=not a.no_gram and not a.no_subsample, naive=a.naive,
+                      stats_impl=a.stats_impl, merge_impl=a.merge_impl, cap_frac_early=a.cap_frac_early)
+    ck = latest_ckpt(ck_dir) if a.resume else None
+    t1 = time.time()
+    seeds = None
+    if ck is not None:
+        st = torch.load(ck, weights_only=False)
+        assert st["args_key"] == _args_key(a), "resume with different run arguments"
+        E = st["atlas"]["E"]
+        start = st["next_batch"]
+    else:
+        if a.edges_from and not a.seed_thresholds:
+            src = torch.load(a.edges_from, map_location="cpu", weights_only=False)
+            E = src["edges"] if "edges" in src else src["atlas"]["E"]
+            Hp = None
+        else:
+            pplan = ds.pilot_plan(plan, a.pilot_tokens, a.tokens_per_batch, a.seed)
+            Hp, _ = pilot(model, ds.batches(vocab, order, a.tokens_per_batch, plan=pplan), dev, 1 << 40)
+            if a.edges_from:
+                src = torch.load(a.edges_from, map_location="cpu", weights_only=False)
+                E = src["edges"] if "edges" in src else src["atlas"]["E"]
+            else:
+                E = torch.cat([pilot_edges([h.to(dev)], probs=tuple(a.edge_q)).cpu() for h in Hp])
+        if a.seed_thresholds:
+            prot = pilot.last_tok // 1024
+            parts = [pilot_seeds([h.to(dev)], E[li:li + 1].to(dev), a.K, a.Kr, n_total, groups=prot)
+                     for li, h in enumerate(Hp)]
+            seeds = (torch.cat([p_[0] for p_ in parts]), torch.cat([p_[1] for p_ in parts]))
+        del Hp
+        start = a.plan_offset
+    t_pilot = time.time() - t1
+    atlas = Atlas(L, D, E, cfg, n_annot=len(ds.vocab) if cfg.subsample else 0, device=dev)
+    if ck is not None:
+        atlas.load_state_dict(st["atlas"])
+        log(f"[atlas] resumed from {ck.name}: batch {start}/{len(plan)}, n_seen {atlas.n_seen}")
+    elif seeds is not None:
+        atlas.seed(*seeds)
+        log(f"[atlas] seeded thresholds for n_total={n_total}: reservoir bins seeded "
+            f"{int((atlas.res_seed != torch.iinfo(torch.int64).min).sum())}/{atlas.res_seed.numel()}")
+    attach(model, atlas.observe)
+    my_plan = plan if world == 1 else plan[rank::world]
+
+    def summary(done: bool, bi: int):
+        return {"args": vars(a), "model": info, "coverage": ds.coverage(order), "n_excluded": n_excluded,
+                "n_batches_plan": len(plan), "next_batch": bi, "complete": done, "world": world,
+                "seconds": {"load": t_load, "pilot": t_pilot, "stream_this_process": time.time() - t2},
+                "n_seen": atlas.n_seen, "stats": atlas.stats}
+
+    logf = open(out / ("batches.jsonl" if world == 1 else f"batches.rank{rank}.jsonl"), "a")
+    ckpt_s, batch_s, last_ckpt_s = 0.0, 0.0, None
+
+    def save_ckpt(next_batch):
+        nonlocal ckpt_s, last_ckpt_s
+        t = time.time()
+        atomic_save({"atlas": atlas.state_dict(), "next_batch": next_batch, "args_key": _args_key(a), "model": info},
+                    ck_dir / f"ckpt_{next_batch}.pt")
+        for old in sorted(ck_dir.glob("ckpt_*.pt"), key=lambda p: int(p.stem.split("_")[1]))[:-2]:
+            old.unlink()
+        if rank == 0:
+            (out / "run.json").write_text(json.dumps(summary(False, next_batch), indent=1))
+        last_ckpt_s = time.time() - t
+        ckpt_s = max(ckpt_s, last_ckpt_s)
+        log(f"[atlas] checkpoint at batch {next_batch}/{len(my_plan)} ({last_ckpt_s:.1f}s)")
+
+    t2 = time.time()
+    n_done = 0
+    with torch.no_grad():
+        src_iter = ds.batches(vocab, order, a.tokens_per_batch, plan=my_plan, start=start)
+        if a.prefetch > 0:
+            src_iter = _prefetch(((b, atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann, device="cpu"))
+                                  for b in src_iter), a.prefetch)
+        else:
+            src_iter = ((b, None) for b in src_iter)
+        for bi, (b, ctx_host) in enumerate(src_iter, start=start):
+            tb = time.time()
+            ids, am = b.input_ids.to(dev, non_blocking=True), b.attention_mask.to(dev, non_blocking=True)
+            fwd_s = None
+            if a.pair_forward or (a.pair_every and bi % a.pair_every == 0):
+                atlas.enabled = False
+                sync(dev)
+                tf0 = time.time()
+                model(input_ids=ids, attention_mask=am)
+                sync(dev)
+                fwd_s = time.time() - tf0
+                atlas.enabled = True
+            ta0 = time.time()
+            ctx = ctx_host.to(dev) if ctx_host is not None else atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann)
+            n_before = atlas.n_seen
+            atlas.begin_batch(ctx)
+            model(input_ids=ids, attention_mask=am)
+            redo = atlas.end_batch()
+            assert redo == []
+            gram_flushed = bi % a.gram_flush_every == a.gram_flush_every - 1
+            if gram_flushed:
+                atlas.flush_gram()
+            sync(dev)
+            atlas_s = time.time() - ta0
+            rec = {"batch": bi, "n_seen_before": n_before, "n_valid": ctx.n_v, "rows": b.n_rows,
+                   "Lmax": int(b.input_ids.shape[1]), "seconds": time.time() - tb, "t_start": tb, "t_end": time.time(),
+                   "fwd_only_s": fwd_s, "atlas_pass_s": atlas_s,
+                   "overhead_vs_fwd": (atlas_s / fwd_s - 1) if fwd_s else None, "gram_flushed": gram_flushed,
+                   "flops": flops_per_batch(info, b.n_rows, b.input_ids.shape[1]), "redo_layers": []}
+            n_done += 1
+            last_ckpt_s = None
+            if (bi + 1) % a.ckpt_every == 0:
+                save_ckpt(bi + 1)
+            rec["ckpt_s"] = last_ckpt_s
+            logf.write(json.dumps(rec) + "\n")
+            logf.flush()
+            batch_s = max(batch_s, rec["seconds"]) if n_done > 2 else batch_s
+            if a.deadline and bi + 1 < len(my_plan) and time.time() > a.deadline - 2 * (batch_s + max(ckpt_s, 30.0)):
+                if (bi + 1) % a.ckpt_every:
+                    save_ckpt(bi + 1)
+                log(f"[atlas] deadline approaching: stopped cleanly at batch {bi + 1}; rerun with --resume")
+                return
+            if a.stop_after and n_done >= a.stop_after:
+                log(f"[atlas] stopping after {n_done} batches (simulated cap)")
+                if rank == 0:
+                    (out / "run.json").write_text(json.dumps(summary(False, bi + 1), indent=1))
+                return
+    logf.close()
+    atlas.check_errors()
+    if world > 1:
+        from .dist import merge_states
+        merge_states(atlas)
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return
+    res = atlas.result()
+    res.update({"model": info, "coverage": ds.coverage(order), "vocab": ds.vocab, "order_seed": a.seed,
+                "n_total_plan": n_total, "n_batches": len(plan)})
+    tf = time.time()
+    atomic_save(res, out / "atlas.pt")
+    final_s = time.time() - tf
+    digests = {k: hashlib.sha256(res[k].contiguous().numpy().tobytes()).hexdigest()
+               for k in ("top_val", "top_tok", "res_tok", "res_val", "res_key", "sub_bin", "enr", "ann_tot", "edges")
+               if k in res}
+    sm = summary(True, len(plan))
+    sm.update({"digests": digests, "final_save_s": final_s, "gram_rows": res.get("gram_rows"),
+               "res_seeded_bins": res["res_seeded_bins"], "res_seed_limited_bins": res["res_seed_limited_bins"],
+               "top_seed_short_groups": res["top_seed_short_groups"]})
+    (out / "run.json").write_text(json.dumps(sm, indent=1))
+    log(f"[atlas] done: final save {final_s:.1f}s; seed verification: {res['res_seed_limited_bins']} of "
+        f"{res['res_seeded_bins']} seeded bins short, top-K groups short {res['top_seed_short_groups']}")
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

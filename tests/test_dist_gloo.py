@@ -1,0 +1,115 @@
+"""Multi-rank protocol on CPU (gloo, world size 2): sharding of the batch plan, and the exact
+cross-rank state combine of proteus_b200.dist.merge_states against the reference's merged result
+(tests/golden/merge_from.npz, two shards merged by the reference's Atlas.merge_from). The row merge
+of the GPU path is replaced by a CPU restatement (the oracle's semantics) so no GPU is needed; a
+rank that fails before the combine makes the other rank's collective end with an error, not hang."""
+from __future__ import annotations
+
+import os
+import socket
+import traceback
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests.harness import golden
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def cpu_row_merge(sc, tok, val, osc, otok, oval):
+    """Row-wise top-K of two sorted states (atlas/core.py:636-643 semantics), CPU."""
+    K = sc.shape[1]
+    allv = torch.cat([sc, osc], 1)
+    idx = torch.argsort(allv, dim=1, descending=True, stable=True)[:, :K]
+    sc.copy_(torch.gather(allv, 1, idx))
+    tok.copy_(torch.gather(torch.cat([tok, otok], 1), 1, idx))
+    val.copy_(torch.gather(torch.cat([val, oval], 1), 1, idx))
+
+
+class _Stats(SimpleNamespace):
+    pass
+
+
+def _shard(z, h):
+    t = lambda k: torch.from_numpy(np.array(z[f"s{h}_{k}"]))  # noqa: E731
+    cfg = SimpleNamespace(K=8, Kr=4, rho_res=0.05, rho_sub=0.2, cap_frac=0.05, seed=11)
+    a = _Stats(top_k=t("top_k"), top_t=t("top_t"), top_s=t("top_s"), res_s=t("res_s"), res_t=t("res_t"),
+               res_v=t("res_v"), sub_sum=t("sub_sum"), sub_sq=t("sub_sq"), sub_bin=t("sub_bin"), E=t("E"),
+               top_seed=t("top_seed"), res_seed=t("res_seed"), enr=t("enr"), ann_tot=t("ann_tot"), n_a=5,
+               n_seen=int(z[f"s{h}_n_seen"]), n_sub=int(z[f"s{h}_n_sub"]), gram=None, cfg=cfg,
+               stats={"batches": 1})
+    return a
+
+
+def _worker(rank, world, port, mode, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import datetime
+        torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
+                                             timeout=datetime.timedelta(seconds=20))
+        from proteus_b200.dist import merge_states, shard_plan
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("injected failure before the combine")
+        z = golden("merge_from")
+        a = _shard(z, rank)
+        merge_states(a, row_merge=cpu_row_merge, gram=False)
+        want = {k[2:]: v for k, v in z.items() if k.startswith("m_")}
+        L, D, K, B, Kr = 2, 48, 8, 5, 4
+        ok = {
+            "top_tok": np.array_equal(a.top_t.view(L, 2, D, K).numpy(), want["top_tok"]),
+            "top_val": np.array_equal((a.top_s.view(L, 2, D, K) * torch.tensor([1., -1.]).view(1, 2, 1, 1)).numpy(),
+                                      want["top_val"]),
+            "res_tok": np.array_equal(a.res_t.view(L, 2, D, B, Kr).numpy(), want["res_tok"]),
+            "res_key": np.array_equal((-a.res_s).view(L, 2, D, B, Kr).numpy(), want["res_key"]),
+            "sub_bin": np.array_equal(a.sub_bin.numpy(), want["sub_bin"]),
+            "enr": np.array_equal(a.enr.numpy(), want["enr"]),
+            "ann_tot": np.array_equal(a.ann_tot.numpy(), want["ann_tot"]),
+            "n": (a.n_seen, a.n_sub) == (int(want["n_seen"]), int(want["n_sub"])),
+            "sums": np.allclose(a.sub_sum.numpy(), want["sub_sum"], rtol=1e-12, atol=1e-9),
+            "shard": sorted(sum((shard_plan(list(range(11)), world, r) for r in range(world)), [])) == list(range(11)),
+        }
+        q.put((rank, ok))
+        torch.distributed.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-400:]}"))
+
+
+def _run(mode, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r, v = q.get(timeout=timeout)
+        out[r] = v
+    for p in ps:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_merge_states_two_ranks_matches_reference():
+    out = _run("ok")
+    for r in (0, 1):
+        assert isinstance(out[r], dict), out[r]
+        assert all(out[r].values()), out[r]
+
+
+def test_failed_rank_ends_combine_with_error_not_hang():
+    out = _run("fail")
+    assert isinstance(out[1], str) and "injected failure" in out[1]
+    assert isinstance(out[0], str), "rank 0 must see an error (timeout or peer loss), not a result"
