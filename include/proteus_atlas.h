@@ -147,9 +147,10 @@ int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t 
  * batch elements that can enter the state's top-K) and, per bin, the Kr smallest keys among rows in
  * the bin under the bin's key ceiling; admitted records are appended to the same lists as
  * atlas_admit. key_order: valid-row indices sorted by key ascending. scratch: device bytes,
- * >= atlas_dense_scratch_bytes(n_v, D, B). flag[0] is set to 1 when the dense path ran.
+ * >= atlas_dense_scratch_bytes(n_v, D, B, dtype) (a column-major copy of the valid rows).
+ * `flag` is unused (kept for ABI stability); K <= 256, Kr <= 256, 2K + 2*B*Kr <= 1024.
  */
-int64_t atlas_dense_scratch_bytes(int64_t n_v, int64_t D, int64_t B);
+int64_t atlas_dense_scratch_bytes(int64_t n_v, int64_t D, int64_t B, int dtype);
 int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, int64_t layer,
                        const int32_t* valid_rows, int64_t n_v, const int64_t* tok, const int64_t* key,
                        const int32_t* key_order, int64_t B, int64_t K, int64_t Kr, int reservoir,

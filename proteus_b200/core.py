@@ -308,7 +308,7 @@ class Atlas:
                 self._R is None or self._R.shape[1] < ctx.n_r or self._R.dtype != self._act_dtype):
             self._R = torch.empty(L, int(ctx.n_r * 1.25) + 1, D, dtype=self._act_dtype, device=dev)
         self._R_used = False
-        sb = load().atlas_dense_scratch_bytes(ctx.n_v, D, B)
+        sb = load().atlas_dense_scratch_bytes(ctx.n_v, D, B, dtype_code(self._act_dtype or torch.float32))
         if self._dense_scratch is None or self._dense_scratch.numel() < sb:
             self._dense_scratch = torch.empty(int(sb * 1.25) + 256, dtype=torch.uint8, device=dev)
 

@@ -52,11 +52,19 @@ struct Vec<DT, 1> {
   __device__ __forceinline__ float at(int) const { return v; }
 };
 
+#ifndef ATLAS_FILTER_U
+#define ATLAS_FILTER_U 4           // rows in flight per lane on the vector paths
+#endif
+#ifndef ATLAS_FILTER_CTAS_PER_SM
+#define ATLAS_FILTER_CTAS_PER_SM 4  // grid = one resident wave of this many 8-warp CTAs per SM
+#endif
+
 constexpr int kWarps = 8;
 constexpr int kStage = 2048;  // staged survivors per CTA (24 KB of shared memory)
+constexpr int kCtasPerSm = ATLAS_FILTER_CTAS_PER_SM;
 
 template <int DT, int VEC, int U>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes, int64_t rows_per_cta,
               const int32_t* __restrict__ rowmap, const float* __restrict__ thr_pos,
               const float* __restrict__ thr_neg, float* __restrict__ out_val, int32_t* __restrict__ out_row,
@@ -95,7 +103,7 @@ filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes
       if (!col_ok) vr[u] = -1;
       if (vr[u] >= 0) x[u].load(H + row * ld_bytes + c0 * (int64_t)sizeof(E));
     }
-    uint32_t bits = 0;
+    uint64_t bits = 0;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (vr[u] < 0) continue;
@@ -103,12 +111,12 @@ filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes
       for (int k = 0; k < VEC; ++k) {
         const float h = x[u].at(k);
         const bool hit = (h > tp[k]) || (h < tn[k]);
-        bits |= (hit ? 1u : 0u) << (u * VEC + k);
+        bits |= (uint64_t)(hit ? 1u : 0u) << (u * VEC + k);
       }
     }
     if (!__any_sync(0xFFFFFFFFu, bits != 0)) continue;
     int total;
-    const int n = __popc(bits);
+    const int n = __popcll(bits);
     const int pre = warp_excl_scan(n, lane, &total);
     int base = 0;
     if (lane == 31) base = atomicAdd(&s_n, total);
@@ -126,7 +134,7 @@ filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes
     for (int u = 0; u < U; ++u) {
 #pragma unroll
       for (int k = 0; k < VEC; ++k) {
-        if (bits & (1u << (u * VEC + k))) {
+        if (bits & (1ull << (u * VEC + k))) {
           if (staged) {
             s_val[slot] = x[u].at(k);
             s_row[slot] = vr[u];
@@ -161,7 +169,7 @@ int launch(const void* H, int64_t T, int64_t D, int64_t ld, const int32_t* rowma
            const float* tn, float* ov, int32_t* orow, int32_t* ocol, int32_t* count, int64_t cap,
            cudaStream_t st) {
   const int64_t strips = (D + 32 * VEC - 1) / (32 * VEC);
-  const int64_t target = (int64_t)num_sms() * 16;          // ~16 CTAs of 8 warps per SM
+  const int64_t target = (int64_t)num_sms() * kCtasPerSm;  // one resident wave of 8-warp CTAs
   int64_t chunks = (target + strips - 1) / strips;
   const int64_t step = (int64_t)kWarps * U;
   int64_t rows = (T + chunks - 1) / chunks;
@@ -198,15 +206,15 @@ extern "C" int atlas_filter_compact(const void* H, int dtype, int64_t T, int64_t
   switch (dtype) {
     case ATLAS_BF16:
       if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0)
-        return launch<ATLAS_BF16, 8, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
+        return launch<ATLAS_BF16, 8, ATLAS_FILTER_U>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
       return launch<ATLAS_BF16, 1, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
     case ATLAS_F16:
       if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0)
-        return launch<ATLAS_F16, 8, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
+        return launch<ATLAS_F16, 8, ATLAS_FILTER_U>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
       return launch<ATLAS_F16, 1, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
     case ATLAS_F32:
       if (D % 4 == 0 && ld % 4 == 0 && a % 16 == 0)
-        return launch<ATLAS_F32, 4, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
+        return launch<ATLAS_F32, 4, ATLAS_FILTER_U>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
       return launch<ATLAS_F32, 1, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
     default:
       return fail(ATLAS_ERR_ARG, "filter: unknown dtype %d", dtype);
