@@ -176,6 +176,23 @@ int atlas_grouped_merge(int64_t* state_sc, int64_t* state_tok, float* state_val,
                         const int32_t* n_dev, int64_t n_max, int32_t* ws_i32, void* ws_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Allocation-free grouped merge. No counterpart in the reference. Same inputs, outputs and result
+ * as atlas_grouped_merge, but the workspace is a fixed device array inside this library instead of
+ * caller memory, for callers that cannot allocate device memory themselves: a host runtime that owns
+ * every device byte through its own pool and forbids side allocations, or a call site that must not
+ * pay for cudaMalloc's implicit device synchronisation in the middle of a stream.
+ * Limits: G <= 262144 groups and n_max <= 262144 records per call (larger requests are rejected
+ * with ATLAS_ERR_ARG); the array (about 11 MB) stays resident on every GPU that loads the library
+ * until the process exits. The first call on a device looks up the array's device address (make it
+ * before any stream capture on that device). All calls share the one array: calls that can overlap
+ * on the GPU (different streams, or devices sharing nothing but this library) race and must be
+ * serialised by the caller. Nothing is allocated, by this call or by anything it calls.
+ */
+int atlas_grouped_merge_static(int64_t* state_sc, int64_t* state_tok, float* state_val, int64_t G, int64_t K,
+                               const int32_t* g, const int64_t* sc, const int64_t* tok, const float* val,
+                               const int32_t* n_dev, int64_t n_max, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Row-wise merge of two sorted states — replaces the top-K / reservoir part of Atlas.merge_from
  * (atlas/core.py:636-643): for each of G rows, (sc, tok, val) <- the K largest of
  * (sc U other_sc) with payloads (keys unique across the two states).

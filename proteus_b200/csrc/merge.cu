@@ -377,3 +377,58 @@ extern "C" int atlas_merge_rows(int64_t* sc, int64_t* tok, float* val, const int
   if (K <= 128) return launch_rows<128>(sc, tok, val, other_sc, other_tok, other_val, G, K, st);
   return launch_rows<256>(sc, tok, val, other_sc, other_tok, other_val, G, K, st);
 }
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free variant of atlas_grouped_merge. Its workspace is this file-scope device array
+// (every GPU that loads the library holds it until the process exits), sized for at most
+// kStaticMergeGroups groups and kStaticMergeRecords candidate records per call.
+namespace atlas {
+namespace {
+constexpr int64_t kStaticMergeGroups = 1 << 18;
+constexpr int64_t kStaticMergeRecords = 1 << 18;
+constexpr int64_t kStaticI32 = 4 * kStaticMergeGroups + 2 * ((kStaticMergeGroups + 2047) / 2048) + 64;
+constexpr int64_t kStaticI32Bytes = (kStaticI32 * 4 + 255) / 256 * 256;
+constexpr int64_t kStaticRecBytes = 3 * ((8 * kStaticMergeRecords + 255) / 256 * 256);
+static __device__ __align__(256) unsigned char g_merge_scratch[kStaticI32Bytes + kStaticRecBytes];
+
+// Device address of g_merge_scratch, looked up once per device (host code only holds a stand-in
+// for the symbol, which must never be handed to a kernel).
+constexpr int kMaxDevices = 64;
+static void* g_scratch_addr[kMaxDevices] = {};
+
+int static_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(ATLAS_ERR_CUDA, "grouped_merge_static: no current CUDA device");
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_merge_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(ATLAS_ERR_CUDA, "grouped_merge_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return ATLAS_OK;
+}
+}  // namespace
+}  // namespace atlas
+
+extern "C" int atlas_grouped_merge_static(int64_t* state_sc, int64_t* state_tok, float* state_val, int64_t G, int64_t K,
+                                          const int32_t* g, const int64_t* sc, const int64_t* tok, const float* val,
+                                          const int32_t* n_dev, int64_t n_max, void* stream) {
+  ATLAS_REQUIRE(G >= 0 && G <= kStaticMergeGroups, "grouped_merge_static: G = %lld exceeds the static workspace limit "
+                "of %lld groups (use atlas_grouped_merge with a caller workspace)", (long long)G,
+                (long long)kStaticMergeGroups);
+  ATLAS_REQUIRE(n_max >= 0 && n_max <= kStaticMergeRecords, "grouped_merge_static: n_max = %lld exceeds the static "
+                "workspace limit of %lld records (use atlas_grouped_merge with a caller workspace)", (long long)n_max,
+                (long long)kStaticMergeRecords);
+  if (G == 0 || n_max == 0) return ATLAS_OK;
+  void* base = nullptr;
+  if (int e = static_scratch(&base)) return e;
+  int32_t* ws_i32 = reinterpret_cast<int32_t*>(base);
+  void* ws_bytes = reinterpret_cast<unsigned char*>(base) + kStaticI32Bytes;
+  // the pipeline clears its per-group counters itself and rebuilds every other workspace field, so
+  // whatever the previous call left in the array does not leak into this one
+  return atlas_grouped_merge(state_sc, state_tok, state_val, G, K, g, sc, tok, val, n_dev, n_max, ws_i32, ws_bytes,
+                             stream);
+}
