@@ -523,12 +523,25 @@ def main():
         e2e_ms = a3.elapsed_time(b3)
         e2e_tokens = sum(c.n_v for _, c in e2e_host)
     atlas.check_errors()
+    combine_ms = None
+    if world > 1:  # exact cross-GPU combine of the shard states (not part of the per-step metric)
+        from proteus_b200.dist import merge_states
+        barrier(world, local)
+        torch.cuda.synchronize()
+        a4, b4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a4.record()
+        merge_states(atlas, gram=False)
+        b4.record()
+        torch.cuda.synchronize()
+        combine_ms = a4.elapsed_time(b4)
 
     ms_max = allreduce(ms, torch.distributed.ReduceOp.MAX if world > 1 else None, world, dev)
     tok_all = allreduce(float(tokens), torch.distributed.ReduceOp.SUM if world > 1 else None, world, dev)
     e2e_max = allreduce(e2e_ms, torch.distributed.ReduceOp.MAX if world > 1 else None, world, dev)
     e2e_tok = allreduce(float(e2e_tokens), torch.distributed.ReduceOp.SUM if world > 1 else None, world, dev)
     fwd_max = allreduce(fwd_ms, torch.distributed.ReduceOp.MAX if world > 1 else None, world, dev)
+    if combine_ms is not None:
+        combine_ms = allreduce(combine_ms, torch.distributed.ReduceOp.MAX, world, dev)
 
     if rank == 0:
         n_filter = kt.count("filter")
@@ -562,6 +575,7 @@ def main():
                 "gram_staged": {"launches": kt.count("gram"), "ms_total": kt.total_ms("gram"),
                                 "rows": kt.work.get("gram", 0)},
                 "gpu_launches": launches, "clocks": clk, "setup_s": setup_s,
+                "combine_ms": combine_ms,
                 "stats_delta": {k: stats1[k] - stats0.get(k, 0) for k in stats1}}
         if not args.no_micro:
             line["kernels"] = kernel_microbench(dev, peaks)

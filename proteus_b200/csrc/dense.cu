@@ -15,6 +15,8 @@
 //      the bin's ceiling), a block scan turns the counts into global ranks, and the first Kr
 //      admissible rows of each bin are emitted. Runs that start above every ceiling stop at once.
 //    Records are staged in shared memory and appended with one atomic per list per CTA.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace atlas {
@@ -43,24 +45,30 @@ __device__ __forceinline__ bool triggered(const int32_t* count, int64_t cap, int
 }
 
 // ---------------------------------------------------------------------------------------- gather
+// Grid-stride over 32x32 tiles (tile t: rows 32*(t % nti), columns 32*(t / nti)) with a grid bounded
+// by the SM count, so the untriggered case costs a few thousand early exits, not one block per tile.
 template <typename T>
 __global__ void dense_gather_kernel(const T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
                                     int64_t n, int64_t n8, T* __restrict__ HT, int64_t ldh,
                                     const int32_t* __restrict__ count, int64_t cap, int force) {
   if (!triggered(count, cap, force)) return;
   __shared__ T tile[32][33];
-  const int64_t i0 = (int64_t)blockIdx.x * 32, d0 = (int64_t)blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
-  for (int k = ty; k < 32; k += 8) {
-    const int64_t i = i0 + k, d = d0 + tx;
-    T v = T(0.0f);
-    if (i < n && d < D) v = H[(int64_t)rows[i] * ld + d];
-    tile[k][tx] = v;
-  }
-  __syncthreads();
-  for (int k = ty; k < 32; k += 8) {
-    const int64_t d = d0 + k, i = i0 + tx;
-    if (d < D && i < n8) HT[d * ldh + i] = tile[tx][k];
+  const int64_t nti = (n8 + 31) / 32, ntiles = nti * ((D + 31) / 32);
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int64_t i0 = (t % nti) * 32, d0 = (t / nti) * 32;
+    for (int k = ty; k < 32; k += 8) {
+      const int64_t i = i0 + k, d = d0 + tx;
+      T v = T(0.0f);
+      if (i < n && d < D) v = H[(int64_t)rows[i] * ld + d];
+      tile[k][tx] = v;
+    }
+    __syncthreads();
+    for (int k = ty; k < 32; k += 8) {
+      const int64_t d = d0 + k, i = i0 + tx;
+      if (d < D && i < n8) HT[d * ldh + i] = tile[tx][k];
+    }
+    __syncthreads();
   }
 }
 
@@ -347,7 +355,8 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   using T = typename Elem<DT>::T;
   const int64_t n8 = (n_v + 7) / 8 * 8;
   T* HT = reinterpret_cast<T*>(scratch);
-  dim3 g1((unsigned)((n8 + 31) / 32), (unsigned)((D + 31) / 32));
+  const int64_t ntiles = (n8 + 31) / 32 * ((D + 31) / 32);
+  const unsigned g1 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)num_sms() * 8));
   dense_gather_kernel<T><<<g1, dim3(32, 8), 0, st>>>(reinterpret_cast<const T*>(H), D, ld, valid_rows, n_v, n8, HT, n8,
                                                      count, cap, force);
   if (int e = check_launch("atlas_dense_select: gather")) return e;

@@ -52,6 +52,12 @@ namespace {
 using namespace tc;
 
 constexpr int kThreads = 192;
+#ifndef ATLAS_GRAM_PAIR
+#define ATLAS_GRAM_PAIR 0  // 1: 256 x 256 Gram tiles on CTA pairs (gram_pair_kernel)
+#endif
+#ifndef ATLAS_GRAM_WIDE
+#define ATLAS_GRAM_WIDE 0  // 1: 128 x 256 Gram tiles (gram_wide_kernel); 0: 128 x 128 tiles
+#endif
 
 // ------------------------------------------------------------------------------------------ Gram
 constexpr int GB = 128;               // output block (M = N = 128)
@@ -177,6 +183,295 @@ gram_tc_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t D, i
   }
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------------------------- Gram (wide)
+// 128 x 256 output tiles: per 64-row chunk the CTA loads 16 KB of A and 32 KB of B for twice the
+// MMA work of a 128 x 128 tile (a third less L2 traffic per FLOP). TMEM holds two 128 x 256 fp32
+// accumulators (all 512 columns) for the segment double buffer; eight epilogue warps split the 256
+// columns so each thread keeps 128 register totals. A tile whose left 128-block lies below the
+// diagonal (block row 2j+1 against column blocks 2j, 2j+1) computes it but never writes it.
+constexpr int WN = 256;
+constexpr int W_STAGES = 4;
+constexpr uint32_t W_TILE_B = WN * GK * 2;  // 32 KB
+constexpr int kWideThreads = 320;           // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+
+struct GramWideSmem {
+  uint8_t a[W_STAGES][G_TILE];
+  uint8_t b[W_STAGES][W_TILE_B];
+  uint64_t full[W_STAGES], empty[W_STAGES], tfull[2], tempty[2];
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void wide_tile(int t, int nb, int& bi, int& bj2) {
+  // tiles in column-superblock order: super-block j holds block rows 0 .. min(nb, 2j+2)-1
+  int j = 0;
+  while (true) {
+    const int rows = min(nb, 2 * j + 2);
+    if (t < rows) break;
+    t -= rows;
+    ++j;
+  }
+  bi = t;
+  bj2 = j;
+}
+
+__global__ void __launch_bounds__(kWideThreads, 1)
+gram_wide_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, int64_t n, int64_t D,
+                 int nb, float* __restrict__ C, uint32_t idesc) {
+  extern __shared__ uint8_t wide_raw[];
+  GramWideSmem& s = *reinterpret_cast<GramWideSmem*>((reinterpret_cast<uintptr_t>(wide_raw) + 1023) & ~uintptr_t(1023));
+  int bi, bj2;
+  wide_tile(blockIdx.x, nb, bi, bj2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (int)((n + GK - 1) / GK);
+  const int nseg = (nk + G_SEG - 1) / G_SEG;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < W_STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], 256);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&s.tmem_base, 512);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tma);
+      prefetch_tmap(&tmb);
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % W_STAGES;
+        const uint32_t ph = (k / W_STAGES) & 1;
+        if (k >= W_STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 111)) break;
+        mbar_arrive_expect_tx(&s.full[st], G_TILE + W_TILE_B);
+        tma_load_2d(s.a[st], &tma, k * GK, bi * GB, &s.full[st]);
+        tma_load_2d(s.b[st], &tmb, k * GK, bj2 * WN, &s.full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % W_STAGES;
+        const uint32_t ph = (k / W_STAGES) & 1;
+        const int seg = k / G_SEG, buf = seg & 1;
+        const bool first = (k % G_SEG) == 0;
+        if (first && seg >= 2 && !mbar_wait(&s.tempty[buf], ((seg >> 1) - 1) & 1, 112)) break;
+        if (!mbar_wait(&s.full[st], ph, 113)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(s.a[st]);
+        const uint32_t b_addr = smem_u32(s.b[st]);
+#pragma unroll
+        for (int kk = 0; kk < GK / 16; ++kk)
+          mma_f16(tmem + buf * WN, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                  (first && kk == 0) ? 0u : 1u);
+        mma_commit(&s.empty[st]);
+        if ((k % G_SEG) == G_SEG - 1 || k == nk - 1) mma_commit(&s.tfull[buf]);
+      }
+    }
+  } else {
+    const int q = warp & 3;             // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;   // 0: columns 0-127, 1: columns 128-255
+    const int row = q * 32 + lane;
+    float tot[GB];
+#pragma unroll
+    for (int c = 0; c < GB; ++c) tot[c] = 0.f;
+    bool ok = true;
+    for (int seg = 0; seg < nseg; ++seg) {
+      const int buf = seg & 1;
+      if (!mbar_wait(&s.tfull[buf], (seg >> 1) & 1, 114)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < GB / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * WN + half * GB + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tot[c * 32 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s.tempty[buf]);
+    }
+    const int bj = 2 * bj2 + half;  // this thread's 128-column block
+    const int64_t gi = (int64_t)bi * GB + row;
+    if (ok && bj >= bi && bj < nb && gi < D) {
+      float* crow = C + gi * D + (int64_t)bj * GB;
+      const int64_t jmax = D - (int64_t)bj * GB;
+      if ((D % 4 == 0) && jmax >= GB) {
+#pragma unroll
+        for (int c = 0; c < GB; c += 4) {
+          float4 v = *reinterpret_cast<float4*>(crow + c);
+          v.x += tot[c]; v.y += tot[c + 1]; v.z += tot[c + 2]; v.w += tot[c + 3];
+          *reinterpret_cast<float4*>(crow + c) = v;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < GB; ++c)
+          if (c < jmax) crow[c] += tot[c];
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------------------------ Gram (CTA pairs)
+// 256 x 256 output tiles on a cluster of two CTAs (the two SMs of a TPC) sharing one
+// tcgen05.mma.cta_group::2 of M = N = 256: CTA r loads rows 128r..128r+127 of the A block and of
+// the B block (32 KB per 64-row chunk, half of what a single-SM 256 x 256 tile would need), the
+// even CTA issues the MMAs, and each CTA's TMEM receives its 128 accumulator rows x 256 columns.
+// Per SM that is the MMA work of a 128 x 256 tile for the operand bytes of a 128 x 128 one.
+//   barriers: full[s] (even CTA; both CTAs' TMA bytes count on it), empty[s] and tfull[b] (one per
+//   CTA, signalled by the even CTA's commits), tempty[b] (even CTA; one arrival per epilogue warp
+//   of both CTAs). TMEM holds two 256-column accumulators (the segment double buffer).
+// Diagonal tiles load their single operand once; the 128-block below the diagonal inside a
+// diagonal tile (CTA 1, left half) is computed but never written.
+constexpr int P_STAGES = 6;
+constexpr int PN = 256;               // tile side (M = N)
+constexpr int kPairThreads = 320;     // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-9 epilogue
+constexpr int kPairEpiWarps = 8;
+
+struct GramPairSmem {
+  uint8_t a[P_STAGES][G_TILE];
+  uint8_t b[P_STAGES][G_TILE];
+  uint64_t full[P_STAGES], empty[P_STAGES], tfull[2], tempty[2];
+  uint32_t tmem_base;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+gram_pair_kernel(const __grid_constant__ CUtensorMap tmap, int64_t n, int64_t D, int nb2, int nb, float* __restrict__ C,
+                 uint32_t idesc) {
+  extern __shared__ uint8_t pair_raw[];
+  GramPairSmem& s = *reinterpret_cast<GramPairSmem*>((reinterpret_cast<uintptr_t>(pair_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t rank = cluster_rank();
+  int t = blockIdx.x >> 1, bi = 0;
+  while (t >= nb2 - bi) {
+    t -= nb2 - bi;
+    ++bi;
+  }
+  const int bj = bi + t;
+  const bool diag = bi == bj;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (int)((n + GK - 1) / GK);
+  const int nseg = (nk + G_SEG - 1) / G_SEG;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P_STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], 2 * kPairEpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(&s.tmem_base, 512);
+  __syncthreads();
+  tc_fence_after();
+  cluster_sync();  // the peer's barriers are initialised before anything signals them
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmap);
+      const uint32_t bytes = 2u * (diag ? G_TILE : 2 * G_TILE);  // both CTAs' loads of one chunk
+      const int32_t arow = bi * PN + (int32_t)rank * GB, brow = bj * PN + (int32_t)rank * GB;
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % P_STAGES;
+        const uint32_t ph = (k / P_STAGES) & 1;
+        if (k >= P_STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 121)) break;
+        if (rank == 0) mbar_arrive_expect_tx(&s.full[st], bytes);
+        const uint32_t fb = cluster_addr(&s.full[st], 0);
+        tma_load_2d_pair(s.a[st], &tmap, k * GK, arow, fb);
+        if (!diag) tma_load_2d_pair(s.b[st], &tmap, k * GK, brow, fb);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % P_STAGES;
+        const uint32_t ph = (k / P_STAGES) & 1;
+        const int seg = k / G_SEG, buf = seg & 1;
+        const bool first = (k % G_SEG) == 0;
+        if (first && seg >= 2 && !mbar_wait(&s.tempty[buf], ((seg >> 1) - 1) & 1, 122)) break;
+        if (!mbar_wait(&s.full[st], ph, 123)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(s.a[st]);
+        const uint32_t b_addr = diag ? a_addr : smem_u32(s.b[st]);
+#pragma unroll
+        for (int kk = 0; kk < GK / 16; ++kk)
+          mma_f16_pair(tmem + buf * PN, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                       (first && kk == 0) ? 0u : 1u);
+        mma_commit_pair(cluster_addr(&s.empty[st], 0));
+        mma_commit_pair(cluster_addr(&s.empty[st], 1));
+        if ((k % G_SEG) == G_SEG - 1 || k == nk - 1) {
+          mma_commit_pair(cluster_addr(&s.tfull[buf], 0));
+          mma_commit_pair(cluster_addr(&s.tfull[buf], 1));
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;            // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;  // 0: columns 0-127 of the tile, 1: columns 128-255
+    const int row = q * 32 + lane;
+    const uint32_t tempty0 = cluster_addr(&s.tempty[0], 0), tempty1 = cluster_addr(&s.tempty[1], 0);
+    float tot[GB];
+#pragma unroll
+    for (int c = 0; c < GB; ++c) tot[c] = 0.f;
+    bool ok = true;
+    for (int seg = 0; seg < nseg; ++seg) {
+      const int buf = seg & 1;
+      if (!mbar_wait(&s.tfull[buf], (seg >> 1) & 1, 124)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < GB / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * PN + half * GB + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tot[c * 32 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(buf ? tempty1 : tempty0);
+    }
+    const int br = 2 * bi + (int)rank, bc = 2 * bj + half;  // 128-blocks of this thread's rows / columns
+    const int64_t gi = (int64_t)br * GB + row;
+    if (ok && bc >= br && bc < nb && gi < D) {
+      float* crow = C + gi * D + (int64_t)bc * GB;
+      const int64_t jmax = D - (int64_t)bc * GB;
+      if ((D % 4 == 0) && jmax >= GB) {
+#pragma unroll
+        for (int c = 0; c < GB; c += 4) {
+          float4 v = *reinterpret_cast<float4*>(crow + c);
+          v.x += tot[c]; v.y += tot[c + 1]; v.z += tot[c + 2]; v.w += tot[c + 3];
+          *reinterpret_cast<float4*>(crow + c) = v;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < GB; ++c)
+          if (c < jmax) crow[c] += tot[c];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // every MMA, TMEM read and remote arrival of both CTAs is done
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, 512);
 }
 
 // ------------------------------------------------------------------------------------------ int8
@@ -329,6 +624,35 @@ extern "C" int atlas_gram_upper(const void* XT, int dtype, int64_t ldx, int64_t 
                            2, (uint64_t)n, (uint64_t)D, (uint64_t)ldx * 2, GK, GB, CU_TENSOR_MAP_SWIZZLE_128B))
     return e;
   const int nb = (int)((D + GB - 1) / GB);
+#if ATLAS_GRAM_PAIR
+  {
+    const int nb2 = (int)((D + PN - 1) / PN);
+    const int64_t tiles = (int64_t)nb2 * (nb2 + 1) / 2;
+    const size_t smem = sizeof(GramPairSmem) + 1024;
+    if (cudaFuncSetAttribute(gram_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return fail(ATLAS_ERR_CUDA, "gram_upper: cannot reserve %zu bytes of shared memory", smem);
+    const uint32_t idesc = dtype == ATLAS_BF16 ? tc::idesc_bf16_f32(PN, PN) : tc::idesc_f16_f32(PN, PN);
+    gram_pair_kernel<<<(unsigned)(2 * tiles), kPairThreads, smem, st>>>(tm, n, D, nb2, nb, C, idesc);
+    return check_launch("atlas_gram_upper");
+  }
+#endif
+#if ATLAS_GRAM_WIDE
+  {
+    CUtensorMap tmb;
+    if (int e = make_tmap_2d(&tmb, XT, dtype == ATLAS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             2, (uint64_t)n, (uint64_t)D, (uint64_t)ldx * 2, GK, WN, CU_TENSOR_MAP_SWIZZLE_128B))
+      return e;
+    const int nb2 = (nb + 1) / 2;
+    int64_t tiles = 0;
+    for (int j = 0; j < nb2; ++j) tiles += (nb < 2 * j + 2 ? nb : 2 * j + 2);
+    const size_t smem = sizeof(GramWideSmem) + 1024;
+    if (cudaFuncSetAttribute(gram_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return fail(ATLAS_ERR_CUDA, "gram_upper: cannot reserve %zu bytes of shared memory", smem);
+    const uint32_t idesc = dtype == ATLAS_BF16 ? tc::idesc_bf16_f32(GB, WN) : tc::idesc_f16_f32(GB, WN);
+    gram_wide_kernel<<<(unsigned)tiles, kWideThreads, smem, st>>>(tm, tmb, n, D, nb, C, idesc);
+    return check_launch("atlas_gram_upper");
+  }
+#endif
   const int64_t tiles = (int64_t)nb * (nb + 1) / 2;
   const size_t smem = sizeof(GramSmem) + 1024;
   if (cudaFuncSetAttribute(gram_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)

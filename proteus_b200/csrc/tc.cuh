@@ -1,4 +1,4 @@
-// sm_100a building blocks: mbarriers with bounded waits, TMA tile loads (no multicast), tcgen05
+// sm_100a building blocks: mbarriers with bounded waits, TMA tile loads (one CTA, own copy), tcgen05
 // MMA / TMEM helpers, and the shared-memory matrix descriptor for K-major 128-byte-swizzled tiles.
 #pragma once
 
@@ -57,7 +57,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   return false;
 }
 
-// 2-D TMA tile load into shared memory, completion counted on `bar` (no multicast).
+// 2-D TMA tile load into shared memory, completion counted on `bar`; each CTA loads its own copy.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
@@ -149,6 +149,72 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
 }
 __host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- CTA pairs (cta_group::2)
+// A cluster of two CTAs on the two SMs of a TPC shares one MMA: the even CTA issues
+// tcgen05.mma.cta_group::2, whose A and B operands are the same shared-memory offsets in both CTAs
+// and whose accumulator rows are split between the two CTAs' TMEM.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier of any CTA of the cluster (address from cluster_addr).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// 2-D TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier that
+// may live in the peer CTA of the pair (bar_cluster from cluster_addr). Own copy, no broadcast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster)
+      : "memory");
+}
+
+// TMEM allocation for a CTA pair: issued by the same warp in both CTAs.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the mbarrier at bar_cluster (either CTA of the pair) once every pair MMA issued so far
+// by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
 }
 
 }  // namespace tc

@@ -70,6 +70,46 @@ def test_filter_large_vector_path():
     assert torch.equal(v[:n], Hf[inv[r[:n]], c[:n]])
 
 
+def test_filter_bf16_threshold_edges():
+    """bf16 path compares packed bf16 pairs against bf16-rounded thresholds; the survivors must be
+    those of the fp32 comparison for thresholds equal to a bf16 value (ties do not survive),
+    one fp32 ulp either side of it, +-inf, beyond the bf16 range, and NaN inputs/thresholds."""
+    KN = _kn()
+    g = torch.Generator(device=DEV).manual_seed(5)
+    T, D = 1536, 1024
+    H = (torch.randn(T, D, generator=g, device=DEV) * 3).to(torch.bfloat16)
+    H[7, :64] = float("nan")
+    H[9, 64:128] = float("inf")
+    H[11, 128:192] = float("-inf")
+    H[13, 192:256] = -0.0
+    Hf = H.float()
+    base = Hf[torch.randint(0, T, (D,), generator=g, device=DEV), torch.arange(D, device=DEV)].abs()
+    tp, tn = base.clone(), base.clone()
+    kind = torch.arange(D, device=DEV) % 8
+    up = lambda x: torch.nextafter(x, torch.full_like(x, float("inf")))  # noqa: E731
+    dn = lambda x: torch.nextafter(x, torch.full_like(x, float("-inf")))  # noqa: E731
+    tp = torch.where(kind == 1, up(tp), tp)
+    tp = torch.where(kind == 2, dn(tp), tp)
+    tn = torch.where(kind == 3, up(tn), tn)
+    tn = torch.where(kind == 4, dn(tn), tn)
+    tp = torch.where(kind == 5, torch.full_like(tp, 3.395e38), tp)  # above the largest bf16
+    tn = torch.where(kind == 5, torch.full_like(tn, float("inf")), tn)
+    tn = torch.where(kind == 6, torch.full_like(tn, float("-inf")), tn)
+    tp = torch.where(kind == 7, torch.full_like(tp, float("-inf")), tp)
+    tp[0::97] = 0.0
+    tn[1::89] = -0.0
+    rowmap = torch.arange(T, dtype=torch.int64, device=DEV)
+    rowmap[3::5] = -1
+    v, r, c, cnt = KN.filter_candidates(H, rowmap, tp, tn, 1 << 22)
+    n = int(cnt)
+    valid = rowmap >= 0
+    mask = ((Hf > tp) | (-Hf > tn)) & valid[:, None]
+    rt, ct = torch.nonzero(mask, as_tuple=True)
+    assert n == rt.numel()
+    key = lambda a, b: (a * D + b).sort().values  # noqa: E731
+    assert torch.equal(key(r[:n], c[:n]), key(rowmap[rt], ct))
+
+
 @pytest.mark.parametrize("case", range(len(STATS_CASES)))
 def test_sub_stats_matches_reference(case):
     """Bin masses and int8 masks bit-exact vs the reference kernel; sums within rtol 1e-5 (the
