@@ -11,7 +11,7 @@
 // hit, so per-step global atomics on the single counter would serialise the whole pass; a warp
 // whose step does not fit the staging area writes directly (global atomic), which keeps the
 // count exact for any survivor density.
-#include "common.cuh"
+#include "tc.cuh"
 
 namespace atlas {
 namespace {
@@ -74,7 +74,10 @@ struct Vec<DT, 1> {
 constexpr int kWX = ATLAS_FILTER_WX;
 constexpr int kWY = ATLAS_FILTER_WY;
 constexpr int kWarps = kWX * kWY;
-constexpr int kStage = 2048;  // staged survivors per CTA (24 KB of shared memory)
+#ifndef ATLAS_FILTER_STAGE
+#define ATLAS_FILTER_STAGE 2048  // staged survivors per CTA (12 bytes each)
+#endif
+constexpr int kStage = ATLAS_FILTER_STAGE;
 constexpr int kCtasPerSm = ATLAS_FILTER_CTAS_PER_SM;
 
 template <int DT, int VEC, int U>
@@ -179,159 +182,438 @@ filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes
   }
 }
 
-// bf16 fast path. Same contract as filter_kernel, three changes:
+// bf16 fast path. Same contract as filter_kernel, built to spend few instructions per byte:
 //  * compares run on packed bf16 pairs against thresholds rounded to bf16 (toward -inf for the
 //    positive pole, toward +inf for the negative pole). For a bf16 value h and an fp32 threshold t,
 //    h > t  <=>  h > rd_bf16(t)  and  h < t  <=>  h < ru_bf16(t) (no bf16 lies strictly between
 //    t and its directed rounding), so the survivors are exactly those of the fp32 comparison;
-//    NaN compares false on both sides as in fp32;
-//  * software pipeline: the U rows of the next step are loaded before the current step is
-//    compared, so every lane keeps 2*U 16-byte loads in flight;
-//  * the row map is read once per 32 rows of a warp (one lane per row, two blocks ahead) and
+//    NaN compares false on both sides as in fp32. Each 32-bit word gives a hit mask (0xFFFF per
+//    surviving half) that is kept for the extraction below;
+//  * survivors are rare (a lane sees one in ~5% of its steps), so a lane with hits takes its
+//    slots one by one with a shared-memory atomic: no warp vote or scan on the common path;
+//  * optional overlap (ATLAS_FILTER_PIPE): flagged rows are parked in shared memory so the next
+//    step's loads go out before the survivors are extracted;
+//  * the row map is read once per 32 rows of a warp (one lane per row, one block ahead) and
 //    handed out with shuffles, so no H load waits on a dependent row-map load.
+#ifndef ATLAS_FILTER_PIPE
+#define ATLAS_FILTER_PIPE 0
+#endif
+
+template <int N>
+struct StageAreaN {
+  static constexpr int kCap = N;
+  float val[N];
+  int32_t row[N], col[N];
+  int n;
+};
+using StageArea = StageAreaN<kStage>;
+
+// One survivor: a staging slot while the area has room, else straight to the global list (the
+// global counter stays exact past `cap`).
+template <class SA>
+__device__ __forceinline__ void emit_one(SA& sa, float h, int32_t row, int32_t col, float* __restrict__ out_val,
+                                         int32_t* __restrict__ out_row, int32_t* __restrict__ out_col,
+                                         int32_t* __restrict__ count, int64_t cap) {
+  const int slot = atomicAdd(&sa.n, 1);
+  if (slot < SA::kCap) {
+    sa.val[slot] = h;
+    sa.row[slot] = row;
+    sa.col[slot] = col;
+  } else {
+    const int64_t g = atomicAdd(count, 1);
+    if (g < cap) {
+      out_val[g] = h;
+      out_row[g] = row;
+      out_col[g] = col;
+    }
+  }
+}
+
+// Hit mask of one 16-byte row vector (8 columns): bit k set when element k survives.
+__device__ __forceinline__ uint32_t hit_bits8(const uint4& x, const __nv_bfloat162 (&tp2)[4],
+                                              const __nv_bfloat162 (&tn2)[4]) {
+  const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+  uint32_t m[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
+    m[w] = __hgt2_mask(h2, tp2[w]) | __hlt2_mask(h2, tn2[w]);
+  }
+  // one byte per element (0x00 / 0xFF), then the byte signs gathered into 8 bits
+  const uint32_t lo = __byte_perm(m[0], m[1], 0x6420), hi = __byte_perm(m[2], m[3], 0x6420);
+  return (((lo & 0x80808080u) * 0x00204081u) >> 28) | ((((hi & 0x80808080u) * 0x00204081u) >> 28) << 4);
+}
+
+// Per-row "any hit" flags of one step of a lane (U row vectors of 8 columns): 3 instructions per
+// 32-bit word, no extraction. Rows with v < 0 (padding) never hit.
+template <int U>
+__device__ __forceinline__ uint32_t bf16_flags(const uint4 (&x)[U], const int32_t (&v)[U], const __nv_bfloat162 (&tp2)[4],
+                                               const __nv_bfloat162 (&tn2)[4]) {
+  uint32_t flags = 0;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const uint32_t w4[4] = {x[u].x, x[u].y, x[u].z, x[u].w};
+    uint32_t a = 0;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
+      a |= __hgt2_mask(h2, tp2[w]) | __hlt2_mask(h2, tn2[w]);
+    }
+    if (a != 0 && v[u] >= 0) flags |= 1u << u;
+  }
+  return flags;
+}
+
+// Survivors of one flagged row vector: rebuild its 8-bit mask and emit them one by one.
+template <class SA>
+__device__ __forceinline__ void bf16_emit_row(const uint4& x, int32_t row, const __nv_bfloat162 (&tp2)[4],
+                                              const __nv_bfloat162 (&tn2)[4], int c0, SA& sa,
+                                              float* __restrict__ out_val, int32_t* __restrict__ out_row,
+                                              int32_t* __restrict__ out_col, int32_t* __restrict__ count, int64_t cap) {
+  uint32_t b = hit_bits8(x, tp2, tn2);
+  while (b) {
+    const int k = __ffs(b) - 1;
+    b &= b - 1;
+    const uint32_t w = k < 2 ? x.x : k < 4 ? x.y : k < 6 ? x.z : x.w;
+    const float h = (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
+    emit_one(sa, h, row, c0 + k, out_val, out_row, out_col, count, cap);
+  }
+}
+
+// Survivors of one step of a lane (rows flagged in `flags`): the 8-bit masks of the flagged rows,
+// ONE shared-memory reservation for all of them, then plain stores. Slots past the staging area go
+// straight to the global list (global atomic per survivor; the count stays exact past `cap`).
+template <int U, class SA>
+__device__ __forceinline__ void bf16_emit_step(uint32_t flags, const uint4 (&x)[U], const int32_t (&v)[U],
+                                               const __nv_bfloat162 (&tp2)[4], const __nv_bfloat162 (&tn2)[4], int c0,
+                                               SA& sa, float* __restrict__ out_val, int32_t* __restrict__ out_row,
+                                               int32_t* __restrict__ out_col, int32_t* __restrict__ count,
+                                               int64_t cap) {
+  uint32_t bits[U];
+  int n = 0;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    bits[u] = (flags & (1u << u)) ? hit_bits8(x[u], tp2, tn2) : 0u;
+    n += __popc(bits[u]);
+  }
+  int slot = atomicAdd(&sa.n, n);
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    uint32_t b = bits[u];
+    while (b) {
+      const int k = __ffs(b) - 1;
+      b &= b - 1;
+      const uint32_t w = k < 2 ? x[u].x : k < 4 ? x[u].y : k < 6 ? x[u].z : x[u].w;
+      const float h = (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
+      if (slot < SA::kCap) {
+        sa.val[slot] = h;
+        sa.row[slot] = v[u];
+        sa.col[slot] = c0 + k;
+      } else {
+        const int64_t g = atomicAdd(count, 1);
+        if (g < cap) {
+          out_val[g] = h;
+          out_row[g] = v[u];
+          out_col[g] = c0 + k;
+        }
+      }
+      ++slot;
+    }
+  }
+}
+
 template <int U>
 __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
-filter_bf16_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes, int64_t rows_per_cta,
+filter_bf16_kernel(const char* __restrict__ H, int T, int D, int64_t ld_bytes, int rows_per_cta,
                    const int32_t* __restrict__ rowmap, const float* __restrict__ thr_pos,
                    const float* __restrict__ thr_neg, float* __restrict__ out_val, int32_t* __restrict__ out_row,
                    int32_t* __restrict__ out_col, int32_t* __restrict__ count, int64_t cap) {
-  static_assert(32 % U == 0 && U * 8 <= 32, "U must divide 32 and give at most 32 hit bits");
+  static_assert(32 % U == 0, "U must divide 32");
   constexpr int kIpb = 32 / U;  // steps per row-map block
   const int lane = threadIdx.x & 31;
   const int warp = (threadIdx.x >> 5) / kWX;
   const int wx = (threadIdx.x >> 5) % kWX;
-  const int64_t c0 = (((int64_t)blockIdx.x * kWX + wx) * 32 + lane) * 8;
-  const bool col_ok = c0 < D;
+  const int c0 = ((blockIdx.x * kWX + wx) * 32 + lane) * 8;  // D < 2^31 (host check)
+  const bool col_ok = c0 < D;  // 8 divides D on this path, so a lane's 8 columns are all in or all out
   __nv_bfloat162 tp2[4], tn2[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
     __nv_bfloat16 p[2], n[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int64_t c = c0 + 2 * w + h;
-      const bool ok = col_ok && c < D;
-      p[h] = __float2bfloat16_rd(ok ? __ldg(thr_pos + c) : __int_as_float(0x7F800000));
-      n[h] = __float2bfloat16_ru(ok ? -__ldg(thr_neg + c) : __int_as_float(0xFF800000));
+      const int c = c0 + 2 * w + h;
+      p[h] = __float2bfloat16_rd(col_ok ? __ldg(thr_pos + c) : __int_as_float(0x7F800000));
+      n[h] = __float2bfloat16_ru(col_ok ? -__ldg(thr_neg + c) : __int_as_float(0xFF800000));
     }
     tp2[w] = __halves2bfloat162(p[0], p[1]);
     tn2[w] = __halves2bfloat162(n[0], n[1]);
   }
-  __shared__ float s_val[kStage];
-  __shared__ int32_t s_row[kStage], s_col[kStage];
-  __shared__ int s_n, s_limit, s_base;
-  if (threadIdx.x == 0) {
-    s_n = 0;
-    s_limit = kStage;
-  }
+  __shared__ StageArea sa;
+  __shared__ int s_base;
+  if (threadIdx.x == 0) sa.n = 0;
   __syncthreads();
-  const int64_t r_begin = (int64_t)blockIdx.y * rows_per_cta;
-  int64_t r_end = r_begin + rows_per_cta;
-  if (r_end > T) r_end = T;
-  const int64_t rbase = r_begin + warp;  // this warp's rows: rbase + j * kWY, j = 0, 1, ...
-  const int64_t n_rows = r_end > rbase ? (r_end - rbase + kWY - 1) / kWY : 0;
-  const int64_t n_steps = (n_rows + U - 1) / U;
-  auto rm_block = [&](int64_t b) -> int32_t {
-    const int64_t row = rbase + (b * 32 + lane) * (int64_t)kWY;
-    return row < r_end ? __ldg(rowmap + row) : -1;
+  const int r_begin = blockIdx.y * rows_per_cta;
+  const int r_end = min(r_begin + rows_per_cta, T);
+  const int rbase = r_begin + warp;  // this warp's rows: rbase + j * kWY, j = 0, 1, ...
+  const int n_rows = r_end > rbase ? (r_end - rbase + kWY - 1) / kWY : 0;
+  const int n_steps = (n_rows + U - 1) / U;
+  auto rm_block = [&](int b) -> int32_t {  // row-map entries of rows b*32 .. b*32+31 of this warp
+    const int row = rbase + (b * 32 + lane) * kWY;
+    return (row < r_end && col_ok) ? __ldg(rowmap + row) : -1;
   };
   int32_t rm_cur = rm_block(0), rm_nxt = rm_block(1);
   const int64_t rstride = (int64_t)kWY * ld_bytes;  // bytes between a warp's consecutive rows
-  const char* p = H + rbase * ld_bytes + c0 * 2;      // row of the step being loaded
-  uint4 xa[U];
-  int32_t va[U];
+  const char* p = H + (int64_t)rbase * ld_bytes + c0 * 2;  // row of the step being loaded
+#if ATLAS_FILTER_PIPE
+  // A lane with hits parks the flagged rows of its step in shared memory, issues the next step's
+  // loads, and extracts the survivors while those loads are in flight.
+  __shared__ uint4 s_x[kWarps * 32][U];
+  __shared__ int32_t s_v[kWarps * 32][U];
+  uint4 x[U];
+  int32_t v[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    va[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, u);
-    if (!col_ok) va[u] = -1;
-    if (va[u] >= 0) xa[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
+    v[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, u);
+    if (v[u] >= 0) x[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
   }
-  for (int64_t it = 0; it < n_steps; ++it) {
-    const int64_t jt = it + 1;  // the step prefetched now
+  for (int it = 0; it < n_steps; ++it) {
+    const uint32_t flags = bf16_flags<U>(x, v, tp2, tn2);
+    if (flags) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (flags & (1u << u)) {
+          s_x[threadIdx.x][u] = x[u];
+          s_v[threadIdx.x][u] = v[u];
+        }
+    }
+    const int jt = it + 1;  // the step loaded now
     if (jt % kIpb == 0) {
       rm_cur = rm_nxt;
       rm_nxt = rm_block(jt / kIpb + 1);
     }
-    const int sub = (int)(jt % kIpb) * U;
+    const int sub = (jt % kIpb) * U;
     p += U * rstride;
-    uint4 xb[U];
-    int32_t vb[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      vb[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, sub + u);
-      if (!col_ok) vb[u] = -1;
-      if (vb[u] >= 0) xb[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
+      v[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, sub + u);
+      if (v[u] >= 0) x[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
     }
-    uint32_t bits = 0;
+    if (flags) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (va[u] < 0) continue;
-      const uint32_t w4[4] = {xa[u].x, xa[u].y, xa[u].z, xa[u].w};
-      uint32_t m[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
-        m[w] = __hgt2_mask(h2, tp2[w]) | __hlt2_mask(h2, tn2[w]);
-      }
-      const uint32_t lo = __byte_perm(m[0], m[1], 0x6420), hi = __byte_perm(m[2], m[3], 0x6420);
-      const uint32_t b = (((lo & 0x80808080u) * 0x00204081u) >> 28) | ((((hi & 0x80808080u) * 0x00204081u) >> 28) << 4);
-      bits |= b << (8 * u);
-    }
-    if (__any_sync(0xFFFFFFFFu, bits != 0)) {
-      int total;
-      const int n = __popc(bits);
-      const int pre = warp_excl_scan(n, lane, &total);
-      int base = 0;
-      if (lane == 31) base = atomicAdd(&s_n, total);
-      base = __shfl_sync(0xFFFFFFFFu, base, 31);
-      const bool staged = base + total <= kStage;
-      if (!staged) {
-        if (lane == 31) {
-          atomicMin(&s_limit, base);
-          base = atomicAdd(count, total);
-        }
-        base = __shfl_sync(0xFFFFFFFFu, base, 31);
-      }
-      int64_t slot = (int64_t)base + pre;
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        uint32_t bu = (bits >> (8 * u)) & 0xFFu;
-        while (bu) {
-          const int k = __ffs(bu) - 1;
-          bu &= bu - 1;
-          const uint32_t w = k < 2 ? xa[u].x : k < 4 ? xa[u].y : k < 6 ? xa[u].z : xa[u].w;
-          const float h = (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
-          if (staged) {
-            s_val[slot] = h;
-            s_row[slot] = va[u];
-            s_col[slot] = (int32_t)(c0 + k);
-          } else if (slot < cap) {
-            out_val[slot] = h;
-            out_row[slot] = va[u];
-            out_col[slot] = (int32_t)(c0 + k);
-          }
-          ++slot;
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      xa[u] = xb[u];
-      va[u] = vb[u];
+      for (int u = 0; u < U; ++u)
+        if (flags & (1u << u))
+          bf16_emit_row(s_x[threadIdx.x][u], s_v[threadIdx.x][u], tp2, tn2, c0, sa, out_val, out_row, out_col, count, cap);
     }
   }
+#else
+  for (int it = 0; it < n_steps; ++it) {
+    if (it > 0 && it % kIpb == 0) {
+      rm_cur = rm_nxt;
+      rm_nxt = rm_block(it / kIpb + 1);
+    }
+    const int sub = (it % kIpb) * U;
+    uint4 x[U];
+    int32_t v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      v[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, sub + u);
+      if (v[u] >= 0) x[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
+    }
+    p += U * rstride;
+    const uint32_t flags = bf16_flags<U>(x, v, tp2, tn2);
+    if (flags) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (flags & (1u << u)) bf16_emit_row(x[u], v[u], tp2, tn2, c0, sa, out_val, out_row, out_col, count, cap);
+    }
+  }
+#endif
   __syncthreads();
-  const int staged_n = s_n < s_limit ? s_n : s_limit;
+  const int staged_n = sa.n < kStage ? sa.n : kStage;  // slots [0, staged_n) are all staged
   if (threadIdx.x == 0) s_base = staged_n > 0 ? atomicAdd(count, staged_n) : 0;
   __syncthreads();
   const int64_t base = s_base;
   for (int i = threadIdx.x; i < staged_n; i += blockDim.x) {
     const int64_t slot = base + i;
     if (slot < cap) {
-      out_val[slot] = s_val[i];
-      out_row[slot] = s_row[i];
-      out_col[slot] = s_col[i];
+      out_val[slot] = sa.val[i];
+      out_row[slot] = sa.row[i];
+      out_col[slot] = sa.col[i];
     }
   }
+}
+
+// ------------------------------------------------------------------ bf16, bulk-copy fed (default)
+// The strip of 256 columns (512 bytes per row) a CTA owns is streamed through a ring of shared
+// memory stages by TMA: one 2-D tile copy of 32 rows x 256 columns (16 KB) per stage, completion
+// counted on an mbarrier. The bytes in flight are bounded by shared memory (kBStages x 16 KB per
+// CTA), not by registers, so HBM sees a deep queue however long the compare-and-emit work of a row
+// takes; one copy per 16 KB keeps the SM's TMA unit far from its issue limit (per-row 512-byte
+// bulk copies saturated it at about half the HBM bandwidth). Warp kBWarps produces (row-map
+// entries four stages ahead; a stage of padding rows only is not copied), warps 0..kBWarps-1
+// consume 4 rows of each stage (one 16-byte vector per lane per row, read from shared memory),
+// release the stage as soon as their vectors are in registers, then compare and emit as
+// filter_bf16_kernel does. Padding rows inside a stage are copied with it and skipped. Every wait is bounded; a wait that gives up records a code in the
+// device status word and the CTA finishes (the producer first waits, again bounded, for the
+// copies it issued).
+#ifndef ATLAS_FILTER_BULK
+#define ATLAS_FILTER_BULK 1
+#endif
+#ifndef ATLAS_FILTER_BSTAGES
+#define ATLAS_FILTER_BSTAGES 3
+#endif
+#ifndef ATLAS_FILTER_BCTAS
+#define ATLAS_FILTER_BCTAS 3
+#endif
+constexpr int kBRows = 32;                       // rows per stage
+constexpr int kBStages = ATLAS_FILTER_BSTAGES;   // stages per CTA
+constexpr int kBWarps = 8;                       // consumer warps (4 rows of a stage each)
+constexpr int kBThreads = (kBWarps + 1) * 32;
+constexpr int kBCtasPerSm = ATLAS_FILTER_BCTAS;
+constexpr int kBSeg = 512;                       // bytes of one row segment (256 bf16 columns)
+constexpr int kBStage = 1024;                    // staged survivors per CTA (12 KB)
+
+struct BulkSmem {
+  uint4 data[kBStages][kBRows][kBSeg / 16];
+  int32_t rows[kBStages][kBRows];
+  uint64_t full[kBStages], empty[kBStages];
+  StageAreaN<kBStage> sa;
+  int s_base;
+};
+
+__global__ void __launch_bounds__(kBThreads, kBCtasPerSm)
+filter_bulk_kernel(const __grid_constant__ CUtensorMap tmap, int T, int D, int rows_per_cta,
+                   const int32_t* __restrict__ rowmap, const float* __restrict__ thr_pos,
+                   const float* __restrict__ thr_neg, float* __restrict__ out_val, int32_t* __restrict__ out_row,
+                   int32_t* __restrict__ out_col, int32_t* __restrict__ count, int64_t cap) {
+  extern __shared__ uint8_t bulk_raw[];
+  BulkSmem& sm = *reinterpret_cast<BulkSmem*>((reinterpret_cast<uintptr_t>(bulk_raw) + 127) & ~uintptr_t(127));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int s0 = blockIdx.x * (kBSeg / 2);  // first column of the strip
+  const int r_begin = blockIdx.y * rows_per_cta;
+  const int r_end = min(r_begin + rows_per_cta, T);
+  const int n_stages = r_end > r_begin ? (r_end - r_begin + kBRows - 1) / kBRows : 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kBStages; ++i) {
+      tc::mbar_init(&sm.full[i], 1);
+      tc::mbar_init(&sm.empty[i], kBWarps);
+    }
+    sm.sa.n = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == kBWarps) {  // producer
+    // row-map entries of this lane's row in stages k .. k+3, loaded four stages ahead so no copy
+    // waits on a dependent row-map load
+    auto rm_at = [&](int k) -> int32_t {
+      const int row = r_begin + k * kBRows + lane;
+      return row < r_end ? __ldg(rowmap + row) : -1;
+    };
+    int32_t rm0 = rm_at(0), rm1 = rm_at(1), rm2 = rm_at(2), rm3 = rm_at(3);
+    int issued = 0;
+    for (int k = 0; k < n_stages; ++k) {
+      const int st = k % kBStages;
+      const uint32_t ph = (uint32_t)(k / kBStages) & 1;
+      // every lane waits (and so acquires the consumers' release); the decision is warp-uniform
+      if (k >= kBStages && !__all_sync(0xFFFFFFFFu, tc::mbar_wait(&sm.empty[st], ph ^ 1, 301))) break;
+      const int32_t vr = rm0;
+      rm0 = rm1;
+      rm1 = rm2;
+      rm2 = rm3;
+      rm3 = rm_at(k + 4);
+      sm.rows[st][lane] = vr;
+      const bool any_valid = __any_sync(0xFFFFFFFFu, vr >= 0);
+      __syncwarp();
+      if (lane == 0) {  // one 2-D tile copy per stage: 32 rows x 256 columns (out-of-range parts read as 0)
+        if (any_valid) {
+          tc::mbar_arrive_expect_tx(&sm.full[st], kBRows * kBSeg);
+          tc::tma_load_2d(&sm.data[st][0][0], &tmap, s0, r_begin + k * kBRows, &sm.full[st]);
+        } else {
+          tc::mbar_arrive(&sm.full[st]);  // a stage of padding rows only: nothing to copy
+        }
+      }
+      issued = k + 1;
+    }
+    if (issued < n_stages && lane == 0) {  // gave up: let the copies already issued land first
+      for (int k = max(0, issued - kBStages); k < issued; ++k)
+        tc::mbar_wait(&sm.full[k % kBStages], (uint32_t)(k / kBStages) & 1, 302);
+    }
+  } else {  // consumers
+    const int c0 = s0 + lane * 8;
+    const bool col_ok = c0 < D;
+    __nv_bfloat162 tp2[4], tn2[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      __nv_bfloat16 p[2], n[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = c0 + 2 * w + h;
+        p[h] = __float2bfloat16_rd(col_ok ? __ldg(thr_pos + c) : __int_as_float(0x7F800000));
+        n[h] = __float2bfloat16_ru(col_ok ? -__ldg(thr_neg + c) : __int_as_float(0xFF800000));
+      }
+      tp2[w] = __halves2bfloat162(p[0], p[1]);
+      tn2[w] = __halves2bfloat162(n[0], n[1]);
+    }
+    constexpr int U = kBRows / kBWarps;
+    for (int k = 0; k < n_stages; ++k) {
+      const int st = k % kBStages;
+      if (!__all_sync(0xFFFFFFFFu, tc::mbar_wait(&sm.full[st], (uint32_t)(k / kBStages) & 1, 303))) break;
+      uint4 x[U];
+      int32_t v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int r = warp + u * kBWarps;
+        v[u] = col_ok ? sm.rows[st][r] : -1;
+        x[u] = sm.data[st][r][lane];
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&sm.empty[st]);
+      const uint32_t flags = bf16_flags<U>(x, v, tp2, tn2);
+      if (flags) bf16_emit_step<U>(flags, x, v, tp2, tn2, c0, sm.sa, out_val, out_row, out_col, count, cap);
+    }
+  }
+  __syncthreads();
+  const int staged_n = sm.sa.n < kBStage ? sm.sa.n : kBStage;  // slots [0, staged_n) are all staged
+  if (threadIdx.x == 0) sm.s_base = staged_n > 0 ? atomicAdd(count, staged_n) : 0;
+  __syncthreads();
+  const int64_t base = sm.s_base;
+  for (int i = threadIdx.x; i < staged_n; i += blockDim.x) {
+    const int64_t slot = base + i;
+    if (slot < cap) {
+      out_val[slot] = sm.sa.val[i];
+      out_row[slot] = sm.sa.row[i];
+      out_col[slot] = sm.sa.col[i];
+    }
+  }
+}
+
+int launch_bulk(const void* H, int64_t T, int64_t D, int64_t ld, const int32_t* rowmap, const float* tp,
+                const float* tn, float* ov, int32_t* orow, int32_t* ocol, int32_t* count, int64_t cap,
+                cudaStream_t st) {
+  const int64_t strips = (D + kBSeg / 2 - 1) / (kBSeg / 2);
+  int64_t chunks = (int64_t)num_sms() * kBCtasPerSm / strips;  // at most one resident wave
+  if (chunks < 1) chunks = 1;
+  int64_t rows = (T + chunks - 1) / chunks;
+  rows = (rows + kBRows - 1) / kBRows * kBRows;
+  chunks = (T + rows - 1) / rows;
+  ATLAS_REQUIRE(strips < 65536 * 32 && chunks < 65536, "filter: grid too large (T=%lld D=%lld)", (long long)T,
+                (long long)D);
+  const size_t smem = sizeof(BulkSmem) + 128;
+  static_assert(kBCtasPerSm * (sizeof(BulkSmem) + 128 + 1024) <= 228 * 1024, "bulk filter: CTAs do not fit an SM");
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(filter_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return fail(ATLAS_ERR_CUDA, "filter: cannot reserve %zu bytes of shared memory", smem);
+    attr_set = true;
+  }
+  CUtensorMap tm;
+  if (int e = make_tmap_2d(&tm, H, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)D, (uint64_t)T, (uint64_t)ld * 2,
+                           kBSeg / 2, kBRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return e;
+  dim3 grid((unsigned)strips, (unsigned)chunks);
+  filter_bulk_kernel<<<grid, kBThreads, smem, st>>>(tm, (int)T, (int)D, (int)rows, rowmap, tp, tn, ov, orow, ocol, count,
+                                                    cap);
+  return check_launch("atlas_filter_compact");
 }
 
 template <int DT, int VEC, int U>
@@ -339,8 +621,11 @@ int launch(const void* H, int64_t T, int64_t D, int64_t ld, const int32_t* rowma
            const float* tn, float* ov, int32_t* orow, int32_t* ocol, int32_t* count, int64_t cap,
            cudaStream_t st) {
   const int64_t strips = (D + 32 * VEC * kWX - 1) / (32 * VEC * kWX);
-  const int64_t target = (int64_t)num_sms() * kCtasPerSm;  // one resident wave of CTAs
-  int64_t chunks = (target + strips - 1) / strips;
+  // At most one resident wave of CTAs: a grid even a few CTAs larger runs those few as a second
+  // wave after the first one and nearly doubles the pass.
+  const int64_t target = (int64_t)num_sms() * kCtasPerSm;
+  int64_t chunks = target / strips;
+  if (chunks < 1) chunks = 1;
   const int64_t step = (int64_t)kWY * U;
   int64_t rows = (T + chunks - 1) / chunks;
   rows = ((rows + step - 1) / step) * step;
@@ -352,8 +637,8 @@ int launch(const void* H, int64_t T, int64_t D, int64_t ld, const int32_t* rowma
   dim3 grid((unsigned)strips, (unsigned)chunks);
   const int64_t ld_bytes = ld * (int64_t)sizeof(typename Elem<DT>::T);
   if constexpr (DT == ATLAS_BF16 && VEC == 8 && ATLAS_FILTER_PACKED)
-    filter_bf16_kernel<U><<<grid, kWarps * 32, 0, st>>>(reinterpret_cast<const char*>(H), T, D, ld_bytes, rows,
-                                                        rowmap, tp, tn, ov, orow, ocol, count, cap);
+    filter_bf16_kernel<U><<<grid, kWarps * 32, 0, st>>>(reinterpret_cast<const char*>(H), (int)T, (int)D, ld_bytes,
+                                                        (int)rows, rowmap, tp, tn, ov, orow, ocol, count, cap);
   else
     filter_kernel<DT, VEC, U><<<grid, kWarps * 32, 0, st>>>(reinterpret_cast<const char*>(H), T, D, ld_bytes, rows,
                                                             rowmap, tp, tn, ov, orow, ocol, count, cap);
@@ -361,6 +646,17 @@ int launch(const void* H, int64_t T, int64_t D, int64_t ld, const int32_t* rowma
 }
 
 }  // namespace
+
+// The bounded waits of this file record into this translation unit's copy of the status word.
+int filter_device_status(int* v, int reset) {
+  if (cudaMemcpyFromSymbol(v, tc::g_device_status, sizeof(int)) != cudaSuccess) return ATLAS_ERR_CUDA;
+  if (reset && *v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(tc::g_device_status, &z, sizeof(int)) != cudaSuccess) return ATLAS_ERR_CUDA;
+  }
+  return ATLAS_OK;
+}
+
 }  // namespace atlas
 
 extern "C" int atlas_filter_compact(const void* H, int dtype, int64_t T, int64_t D, int64_t ld,
@@ -374,13 +670,16 @@ extern "C" int atlas_filter_compact(const void* H, int dtype, int64_t T, int64_t
   if (T == 0 || D == 0) return ATLAS_OK;
   ATLAS_REQUIRE(H && rowmap && thr_pos && thr_neg && count, "filter: null pointer");
   ATLAS_REQUIRE(cap == 0 || (out_val && out_row && out_col), "filter: null output");
-  ATLAS_REQUIRE(D < (1LL << 31), "filter: D too large");
+  ATLAS_REQUIRE(D < (1LL << 30) && T < (1LL << 30), "filter: T or D too large (T=%lld D=%lld)", (long long)T, (long long)D);
   cudaStream_t st = (cudaStream_t)stream;
   const uintptr_t a = (uintptr_t)H;
   switch (dtype) {
     case ATLAS_BF16:
-      if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0)
+      if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0) {
+        if (ATLAS_FILTER_BULK)
+          return launch_bulk(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
         return launch<ATLAS_BF16, 8, ATLAS_FILTER_U>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
+      }
       return launch<ATLAS_BF16, 1, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
     case ATLAS_F16:
       if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0)

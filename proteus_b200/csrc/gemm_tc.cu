@@ -56,7 +56,7 @@ constexpr int kThreads = 192;
 #define ATLAS_GRAM_PAIR 0  // 1: 256 x 256 Gram tiles on CTA pairs (gram_pair_kernel)
 #endif
 #ifndef ATLAS_GRAM_WIDE
-#define ATLAS_GRAM_WIDE 0  // 1: 128 x 256 Gram tiles (gram_wide_kernel); 0: 128 x 128 tiles
+#define ATLAS_GRAM_WIDE 2  // 128 x 256 Gram tiles (gram_wide_kernel): 1 always, 0 never, 2 when they fill a wave
 #endif
 
 // ------------------------------------------------------------------------------------------ Gram
@@ -597,16 +597,23 @@ int gram_upper_f32(const float* XT, int64_t ldx, int64_t n, int64_t D, float* C,
 
 using namespace atlas;
 
+namespace atlas {
+int filter_device_status(int* v, int reset);  // filter.cu's bounded waits
+}
+
+// Status of the bounded waits: the first code recorded by the tensor-core kernels (this file) or,
+// when they recorded none, by the bulk-fed filter (filter.cu); each file keeps its own word.
 extern "C" int atlas_device_status(int* status_host, int reset) {
-  int v = 0;
+  int v = 0, vf = 0;
   if (cudaMemcpyFromSymbol(&v, tc::g_device_status, sizeof(int)) != cudaSuccess)
     return fail(ATLAS_ERR_CUDA, "device_status: read failed");
-  if (status_host) *status_host = v;
   if (reset && v) {
     const int z = 0;
     if (cudaMemcpyToSymbol(tc::g_device_status, &z, sizeof(int)) != cudaSuccess)
       return fail(ATLAS_ERR_CUDA, "device_status: reset failed");
   }
+  if (atlas::filter_device_status(&vf, reset) != ATLAS_OK) return fail(ATLAS_ERR_CUDA, "device_status: read failed");
+  if (status_host) *status_host = v ? v : vf;
   return ATLAS_OK;
 }
 
@@ -636,23 +643,24 @@ extern "C" int atlas_gram_upper(const void* XT, int dtype, int64_t ldx, int64_t 
     return check_launch("atlas_gram_upper");
   }
 #endif
-#if ATLAS_GRAM_WIDE
-  {
+  // 128 x 256 tiles move a third fewer operand bytes per FLOP than 128 x 128 ones (the narrow
+  // tiles are L2-to-SM bound at about half the tensor peak), but they come in half the number: use
+  // them once they fill at least one wave of the GPU.
+  const int nb2w = (nb + 1) / 2;
+  int64_t wide_tiles = 0;
+  for (int j = 0; j < nb2w; ++j) wide_tiles += (nb < 2 * j + 2 ? nb : 2 * j + 2);
+  if (ATLAS_GRAM_WIDE == 1 || (ATLAS_GRAM_WIDE == 2 && wide_tiles >= num_sms())) {
     CUtensorMap tmb;
     if (int e = make_tmap_2d(&tmb, XT, dtype == ATLAS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                              2, (uint64_t)n, (uint64_t)D, (uint64_t)ldx * 2, GK, WN, CU_TENSOR_MAP_SWIZZLE_128B))
       return e;
-    const int nb2 = (nb + 1) / 2;
-    int64_t tiles = 0;
-    for (int j = 0; j < nb2; ++j) tiles += (nb < 2 * j + 2 ? nb : 2 * j + 2);
     const size_t smem = sizeof(GramWideSmem) + 1024;
     if (cudaFuncSetAttribute(gram_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return fail(ATLAS_ERR_CUDA, "gram_upper: cannot reserve %zu bytes of shared memory", smem);
     const uint32_t idesc = dtype == ATLAS_BF16 ? tc::idesc_bf16_f32(GB, WN) : tc::idesc_f16_f32(GB, WN);
-    gram_wide_kernel<<<(unsigned)tiles, kWideThreads, smem, st>>>(tm, tmb, n, D, nb, C, idesc);
+    gram_wide_kernel<<<(unsigned)wide_tiles, kWideThreads, smem, st>>>(tm, tmb, n, D, nb, C, idesc);
     return check_launch("atlas_gram_upper");
   }
-#endif
   const int64_t tiles = (int64_t)nb * (nb + 1) / 2;
   const size_t smem = sizeof(GramSmem) + 1024;
   if (cudaFuncSetAttribute(gram_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)

@@ -129,7 +129,7 @@ def test_sub_stats_matches_reference(case):
     assert (np.abs(sq.cpu().numpy() - (Xd ** 2).sum(0)) <= 1e-6 * (Xd ** 2).sum(0) + 1e-12).all()
 
 
-@pytest.mark.parametrize("n,D", [(1600, 5120), (301, 1000), (77, 96), (4096, 640)])
+@pytest.mark.parametrize("n,D", [(1600, 5120), (301, 1000), (77, 96), (4096, 640), (700, 3900)])
 def test_gram_upper_blocks(n, D):
     """gram_accumulate semantics: two accumulations, rel-max error < 1e-5 vs fp64 (reference
     test tolerance, tests/test_stats_triton.py:74), lower 128-blocks untouched."""
