@@ -35,6 +35,10 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+# DRAM bytes (read + write) per row of H of one filter launch, from the ncu capture of the C2 case
+# (dram__bytes_read.sum + dram__bytes_write.sum = 167.92 MB + 5.62 MB over 16384 rows of 5120 bf16
+# columns at 0.3% survivors); the filter's traffic grows with the rows it streams.
+FILTER_DRAM_BYTES_PER_ROW = (167.919872e6 + 5.618176e6) / 16384
 METRIC = "ESM-2 650M atlas tokens/s"
 L_650M, D_650M = 33, 5120
 
@@ -124,6 +128,12 @@ class KernelTimer:
 
     def count(self, name):
         return len(self.ev.get(name, []))
+
+    def quantiles_ms(self, name):
+        t = sorted(a.elapsed_time(b) for a, b in self.ev.get(name, []))
+        if not t:
+            return None
+        return {"min": t[0], "median": t[len(t) // 2], "max": t[-1]}
 
 
 def dist_setup(n_gpus):
@@ -239,8 +249,10 @@ def step(model, atlas, ids, am, ctx):
 # ----------------------------------------------------------------------------- kernel micro-benchmarks
 @torch.no_grad()
 def kernel_microbench(dev, peaks, reps=20):
-    """C2 filter pass ([16384, 5120] bf16, heavy-tailed, thresholds at the 99.9% column quantile)
-    and C3 Gram (16 accumulations of 16384 x 5120 bf16 rows): achieved GB/s and TFLOP/s."""
+    """Kernel-level configs: C2 filter pass ([16384, 5120] bf16, heavy-tailed, thresholds at the
+    99.9% column quantile), C3 Gram (one of 16 accumulations of 16384 x 5120 bf16 rows), C3 stats
+    and int8 enrichment GEMM (16384 staged rows), C2 top-K merge (one block's candidates into one
+    layer's state): achieved GB/s, TFLOP/s, TOP/s against the measured peaks."""
     from proteus_b200 import kernels as KN
     out = {}
     g = torch.Generator(device=dev).manual_seed(7)
@@ -293,6 +305,76 @@ def kernel_microbench(dev, peaks, reps=20):
     flops = D * D * n  # upper-triangle convention (tune_stats.py:74): D^2 * n per accumulation
     out["gram_c3"] = {"D": D, "rows_per_call": n, "ms_per_call": ms, "TFLOPs": flops / ms / 1e9,
                       "frac_bf16": flops / ms / 1e9 / peaks["bf16_tflops"]}
+    del C
+
+    def timed(fn, reps_=reps):
+        fn()
+        torch.cuda.synchronize()
+        ev = []
+        for _ in range(reps_):
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record()
+            fn()
+            b_.record()
+            ev.append((a_, b_))
+        torch.cuda.synchronize()
+        return statistics.median([x.elapsed_time(y) for x, y in ev])
+
+    # C3 subsample stats: one call over 16384 staged rows (bins, sums, int8 masks of 3 levels x 2 poles)
+    t3 = torch.distributions.StudentT(torch.tensor(3.0, device=dev)).sample((n, D))
+    Xs = (t3 * scale + shift).to(torch.bfloat16)
+    del t3
+    qs = torch.tensor([0.5, 0.9, 0.99, 0.999, 0.9999], device=dev)
+    E0 = torch.quantile(Xs[:2048].float(), qs, dim=0).T.contiguous()
+    E1 = torch.quantile(-Xs[:2048].float(), qs, dim=0).T.contiguous()
+    XT.copy_(Xs.T)
+    del Xs
+    levels, NL, B = [2, 3, 4], 3, 5
+    s_ = torch.zeros(D, device=dev, dtype=torch.float64)
+    sq_ = torch.zeros(D, device=dev, dtype=torch.float64)
+    bins_ = torch.zeros(2, D, B, device=dev, dtype=torch.int64)
+    masks = torch.zeros(2, NL, D, n, device=dev, dtype=torch.int8)
+    ms = timed(lambda: KN.sub_stats_into(XT, 0, n, E0, E1, levels, s_, sq_, bins_, masks, n))
+    bytes_ = D * n * 2 + 2 * NL * D * n + D * (2 * B * 4 + 2 * 8 * 2 + 2 * B * 8 * 2)
+    out["stats_c3"] = {"D": D, "rows_per_call": n, "ms_per_call": ms, "bytes": bytes_, "GBps": bytes_ / ms / 1e6,
+                       "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"]}
+    del XT
+    # C3 int8 enrichment GEMM: masks [2*3*D, 16384] x one-hot labels [32, 16384] (Zipf s=1.1 classes)
+    A = 32
+    zipf = 1.0 / torch.arange(1, A + 1, device=dev, dtype=torch.float64) ** 1.1
+    lab = torch.multinomial(zipf / zipf.sum(), n, replacement=True, generator=g)
+    annT = torch.zeros(A, n, device=dev, dtype=torch.int8)
+    annT[lab, torch.arange(n, device=dev)] = 1
+    M = 2 * NL * D
+    cnt_out = torch.zeros(M, A, device=dev, dtype=torch.int64)
+    m2 = masks.view(M, n)
+    ms = timed(lambda: KN.count_gemm_i8(m2, annT, cnt_out, A))
+    ops = 2 * M * n * A
+    bytes_ = M * n + A * n + M * A * 8 * 2
+    out["i8_c3"] = {"M": M, "K": n, "N": A, "ms_per_call": ms, "TOPs": ops / ms / 1e9, "bytes": bytes_,
+                    "GBps": bytes_ / ms / 1e6, "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"]}
+    del masks, m2, cnt_out
+    # C2 top-K merge: one block's candidates (~0.2% of 16384 x 5120, random keys) into the [10240, 100]
+    # state of one layer (2 poles x 5120 columns), sorted rows, fresh candidates every call
+    G, K = 2 * D, 100
+    n_c = 168_000
+    st_sc = torch.full((G, K), torch.iinfo(torch.int64).min, device=dev, dtype=torch.int64)
+    st_tok = torch.full((G, K), -1, device=dev, dtype=torch.int64)
+    st_val = torch.full((G, K), float("-inf"), device=dev)
+    sets = []
+    for i in range(reps + 2):
+        gi = torch.randint(0, G, (n_c,), device=dev, generator=g, dtype=torch.int32)
+        sci = torch.randint(-(1 << 62), 1 << 62, (n_c,), device=dev, generator=g, dtype=torch.int64)
+        toki = torch.randint(0, 1 << 32, (n_c,), device=dev, generator=g, dtype=torch.int64)
+        vali = torch.randn(n_c, device=dev, generator=g)
+        sets.append((gi, sci, toki, vali))
+    n_dev = torch.tensor([n_c], device=dev, dtype=torch.int32)
+    KN.grouped_merge_records(st_sc, st_tok, st_val, K, *sets[0], n_dev, n_c)  # fill the state
+    it = iter(sets[1:])
+    ms = timed(lambda: KN.grouped_merge_records(st_sc, st_tok, st_val, K, *next(it), n_dev, n_c))
+    bytes_ = n_c * 24 + G * K * 20 * 2
+    out["merge_c2"] = {"G": G, "K": K, "candidates": n_c, "ms_per_call": ms, "bytes": bytes_,
+                       "GBps": bytes_ / ms / 1e6, "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"]}
     return out
 
 
@@ -570,8 +652,11 @@ def main():
                         "d2h_bytes_per_step": 32},
                 "roofline": {"kernel": "atlas_filter_compact (K1)", "bound": "hbm", "achieved": achieved,
                              "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                             "traffic": None, "ms_per_launch": filt_ms, "launches": n_filter,
-                             "algorithmic_bytes_per_launch": bytes_launch, "peak_source": peaks["source"]},
+                             "traffic": FILTER_DRAM_BYTES_PER_ROW * rows / K,
+                             "traffic_source": "ncu dram read+write of one C2 launch (16384 rows), scaled by rows",
+                             "ms_per_launch": filt_ms, "launch_ms_quantiles": kt.quantiles_ms("filter"),
+                             "launches": n_filter, "algorithmic_bytes_per_launch": bytes_launch,
+                             "peak_source": peaks["source"]},
                 "gram_staged": {"launches": kt.count("gram"), "ms_total": kt.total_ms("gram"),
                                 "rows": kt.work.get("gram", 0)},
                 "gpu_launches": launches, "clocks": clk, "setup_s": setup_s,

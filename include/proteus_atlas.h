@@ -32,9 +32,10 @@ enum atlas_status {
   ATLAS_ERR_UNSUPPORTED = 3
 };
 
-/* Device status word of the tensor-core kernels: 0, or the code of the first bounded wait that gave
- * up (a kernel never hangs; it records the failure here and finishes). Synchronous read; `reset`
- * clears it. No counterpart in the reference (its Triton kernels have no waits). */
+/* Device status word of the kernels that wait on mbarriers (the tensor-core kernels and the TMA-fed
+ * filter): 0, or the code of the first bounded wait that gave up (a kernel never hangs; it records
+ * the failure here and finishes). Synchronous read; `reset` clears it. No counterpart in the
+ * reference (its Triton kernels have no waits). */
 int atlas_device_status(int* status_host, int reset);
 
 /* Message of the last error raised on the calling host thread ("" if none). */
