@@ -423,6 +423,15 @@ def cpu_oracle_run(steps, warmup, layers=1, seed=11):
     """Time the numpy oracle (reference algorithm, stats v1 + merge loop) on `layers` layers of the
     C4 shape in the seeded steady state; returns tokens/s for the full 33-layer atlas."""
     from oracle import atlas_np as O
+    # every host core, whatever torchrun set OMP_NUM_THREADS to (it sets 1 per rank): the oracle's
+    # thread pool and numpy's BLAS both get the whole affinity set
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    os.environ["ORACLE_THREADS"] = str(cores)
+    try:
+        from threadpoolctl import threadpool_limits
+        blas = threadpool_limits(limits=cores)
+    except Exception:  # noqa: BLE001  threadpoolctl missing: numpy keeps its own setting
+        blas = None
     n_b = warmup + steps
     data = cpu_sample_stream(n_b, layers, seed)
     E, ts, rk = cpu_sample_seeds(layers, seed)
@@ -448,7 +457,9 @@ def cpu_oracle_run(steps, warmup, layers=1, seed=11):
             toks.append(valid.size)
     per_tok_layer = sum(times) / (sum(toks) * layers)
     value = 1.0 / (per_tok_layer * L_650M)
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    threads = cores
+    if blas is not None:
+        blas.restore_original_limits()
     sample = (f"numpy oracle of the reference atlas (stats v1, merge loop), {len(times)} batches x {layers} of 33 "
               f"layers, [32768 x 5120] synthetic heavy-tailed activations, K=100 Kr=32, seeded; extrapolated to 33 "
               f"layers; forward not included")

@@ -176,12 +176,131 @@ sub_stats_kernel(const typename Elem<DT>::T* __restrict__ XT, int64_t ldx, int64
   }
 }
 
+// bf16 path of the same statistics, on packed pairs: every edge compare is one bf16x2 compare per
+// two rows against the edge rounded to bf16 (up for the positive pole x >= E0; down for the
+// negative pole, x <= -E1), which for bf16 values is exactly the fp32 compare: no bf16 lies
+// strictly between an fp32 edge and its directed rounding. Counts come from popcounts of the
+// compare masks (16 set bits per counted row), and a level's int8 mask reuses the compare words of
+// its edge. Sums stay fp32 within the 8-row vector and fp64 across vectors.
+__global__ void __launch_bounds__(256)
+sub_stats_bf16_kernel(const __nv_bfloat16* __restrict__ XT, int64_t ldx, int64_t col0, int64_t n, int64_t D,
+                      const float* __restrict__ E0, const float* __restrict__ E1, int B, Levels lev, int NL,
+                      double* __restrict__ sum, double* __restrict__ sq, int64_t* __restrict__ bins,
+                      int8_t* __restrict__ masks, int64_t n_pad) {
+  const int lane = threadIdx.x & 31;
+  const int64_t d = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (d >= D) return;
+  __nv_bfloat162 pe[kMaxB], ne[kMaxB];
+  uint32_t levmask[kMaxB];  // bit j set when level j sits on edge b
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) {
+    const bool ok = b < B;
+    pe[b] = __bfloat162bfloat162(__float2bfloat16_ru(ok ? E0[d * B + b] : __int_as_float(0x7F800000)));
+    ne[b] = __bfloat162bfloat162(__float2bfloat16_rd(ok ? -E1[d * B + b] : __int_as_float(0xFF800000)));
+    uint32_t lm = 0;
+#pragma unroll
+    for (int j = 0; j < kMaxNL; ++j)
+      if (j < NL && lev.v[j] == b) lm |= 1u << j;
+    levmask[b] = lm;
+  }
+  int c0[kMaxB], c1[kMaxB];
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) c0[b] = c1[b] = 0;
+  double acc_s = 0.0, acc_q = 0.0;
+  const __nv_bfloat16* col = XT + d * ldx + col0;
+  const int64_t n_loop = masks ? n_pad : n;
+  for (int64_t i = (int64_t)lane * 8; i < n_loop; i += 256) {
+    uint32_t w4[4], vm[4];
+    if (i + 8 <= n) {
+      const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(col + i));
+      w4[0] = raw.x; w4[1] = raw.y; w4[2] = raw.z; w4[3] = raw.w;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) vm[w] = 0xFFFFFFFFu;
+    } else {  // the ragged end of the column (and mask padding past n): rows >= n are zero, uncounted
+      const unsigned short* c16 = reinterpret_cast<const unsigned short*>(col);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int64_t r = i + 2 * w;
+        const uint32_t lo = r < n ? c16[r] : 0u, hi = r + 1 < n ? c16[r + 1] : 0u;
+        w4[w] = lo | (hi << 16);
+        vm[w] = (r < n ? 0x0000FFFFu : 0u) | (r + 1 < n ? 0xFFFF0000u : 0u);
+      }
+    }
+    float s32 = 0.0f, q32 = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float lo = __uint_as_float(w4[w] << 16), hi = __uint_as_float(w4[w] & 0xFFFF0000u);
+      s32 += lo;
+      s32 += hi;
+      q32 = fmaf(lo, lo, q32);
+      q32 = fmaf(hi, hi, q32);
+    }
+    acc_s += (double)s32;
+    acc_q += (double)q32;
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      if (b >= B) break;
+      uint32_t mp[4], mn[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
+        mp[w] = __hge2_mask(h2, pe[b]) & vm[w];
+        mn[w] = __hle2_mask(h2, ne[b]) & vm[w];
+      }
+      c0[b] += __popc(mp[0]) + __popc(mp[1]) + __popc(mp[2]) + __popc(mp[3]);
+      c1[b] += __popc(mn[0]) + __popc(mn[1]) + __popc(mn[2]) + __popc(mn[3]);
+      uint32_t lm = masks ? levmask[b] : 0u;
+      if (lm) {  // one byte (0/1) per row, rows i..i+7 little-endian in one 8-byte store
+        const uint64_t wp = (uint64_t)(__byte_perm(mp[0], mp[1], 0x6420) & 0x01010101u) |
+                            ((uint64_t)(__byte_perm(mp[2], mp[3], 0x6420) & 0x01010101u) << 32);
+        const uint64_t wn = (uint64_t)(__byte_perm(mn[0], mn[1], 0x6420) & 0x01010101u) |
+                            ((uint64_t)(__byte_perm(mn[2], mn[3], 0x6420) & 0x01010101u) << 32);
+        while (lm) {
+          const int j = __ffs(lm) - 1;
+          lm &= lm - 1;
+          *reinterpret_cast<uint64_t*>(masks + ((int64_t)(0 * NL + j) * D + d) * n_pad + i) = wp;
+          *reinterpret_cast<uint64_t*>(masks + ((int64_t)(1 * NL + j) * D + d) * n_pad + i) = wn;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc_s += __shfl_xor_sync(0xFFFFFFFFu, acc_s, o);
+    acc_q += __shfl_xor_sync(0xFFFFFFFFu, acc_q, o);
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      c0[b] += __shfl_xor_sync(0xFFFFFFFFu, c0[b], o);
+      c1[b] += __shfl_xor_sync(0xFFFFFFFFu, c1[b], o);
+    }
+  }
+  if (lane == 0) {
+    sum[d] += acc_s;
+    sq[d] += acc_q;
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      if (b >= B) break;
+      const int nx0 = (b + 1 < B) ? c0[b + 1] : 0;
+      const int nx1 = (b + 1 < B) ? c1[b + 1] : 0;
+      bins[d * B + b] += (int64_t)((c0[b] - nx0) >> 4);  // 16 mask bits per counted row
+      bins[(D + d) * B + b] += (int64_t)((c1[b] - nx1) >> 4);
+    }
+  }
+}
+
 template <int DT>
 int launch_stats(const void* XT, int64_t ldx, int64_t col0, int64_t n, int64_t D, const float* E0, const float* E1,
                  int64_t B, const Levels& lev, int64_t NL, double* sum, double* sq, int64_t* bins, int8_t* masks,
                  int64_t n_pad, cudaStream_t st) {
   const int warps = 8;
   dim3 grid((unsigned)((D + warps - 1) / warps));
+  if constexpr (DT == ATLAS_BF16) {
+    if ((uintptr_t)XT % 16 == 0) {
+      sub_stats_bf16_kernel<<<grid, warps * 32, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(XT), ldx, col0, n, D, E0,
+                                                         E1, (int)B, lev, (int)NL, sum, sq, bins, masks, n_pad);
+      return check_launch("atlas_sub_stats");
+    }
+  }
   sub_stats_kernel<DT><<<grid, warps * 32, 0, st>>>(reinterpret_cast<const typename Elem<DT>::T*>(XT), ldx, col0, n, D,
                                                      E0, E1, (int)B, lev, (int)NL, sum, sq, bins, masks, n_pad);
   return check_launch("atlas_sub_stats");

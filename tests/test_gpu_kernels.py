@@ -129,6 +129,47 @@ def test_sub_stats_matches_reference(case):
     assert (np.abs(sq.cpu().numpy() - (Xd ** 2).sum(0)) <= 1e-6 * (Xd ** 2).sum(0) + 1e-12).all()
 
 
+def test_sub_stats_bf16_edge_ties():
+    """bf16 statistics compare packed pairs against edges rounded to bf16; counts and masks must be
+    those of the fp32 compares for edges equal to values present in X (ties count: x >= E0,
+    -x >= E1), one fp32 ulp either side, and +-0 / +-inf / NaN rows; a ragged n and mask padding."""
+    KN = _kn()
+    g = torch.Generator().manual_seed(9)
+    n, D, B = 1001, 136, 5
+    X = (torch.randn(n, D, generator=g) * 2).to(torch.bfloat16)
+    X[3, :8] = float("nan")
+    X[5, 8:16] = float("inf")
+    X[6, 16:24] = float("-inf")
+    X[7, 24:32] = -0.0
+    X[8, 24:32] = 0.0
+    Xf = X.float()
+    pick = lambda: Xf[torch.randint(0, n, (D,), generator=g), torch.arange(D)].nan_to_num(0.0, 0.0, 0.0)  # noqa: E731
+    E0 = torch.stack([pick() for _ in range(B)], 1).sort(1).values
+    E1 = torch.stack([-pick() for _ in range(B)], 1).sort(1).values
+    up = lambda x: torch.nextafter(x, torch.full_like(x, float("inf")))  # noqa: E731
+    dn = lambda x: torch.nextafter(x, torch.full_like(x, float("-inf")))  # noqa: E731
+    E0[1::3, 1], E0[2::3, 3] = up(E0[1::3, 1]), dn(E0[2::3, 3])
+    E1[0::3, 2], E1[2::3, 4] = up(E1[0::3, 2]), dn(E1[2::3, 4])
+    E0[:, 0] = torch.where(torch.arange(D) % 5 == 0, torch.zeros(D), E0[:, 0])
+    E0, E1 = E0.sort(1).values.contiguous(), E1.sort(1).values.contiguous()
+    levels = (2, 3, 4)
+    s, sq, cnt, M = KN.sub_stats(X.to(DEV), E0.to(DEV), E1.to(DEV), levels)
+    ge0 = Xf[:, :, None] >= E0[None]  # [n, D, B]
+    ge1 = (-Xf)[:, :, None] >= E1[None]
+    cum0, cum1 = ge0.sum(0), ge1.sum(0)  # [D, B]
+    nxt = lambda c: torch.cat([c[:, 1:], torch.zeros(D, 1, dtype=c.dtype)], 1)  # noqa: E731
+    want_cnt = torch.stack([cum0 - nxt(cum0), cum1 - nxt(cum1)]).to(torch.int32)
+    assert torch.equal(cnt.cpu(), want_cnt)
+    n8 = -(-n // 8) * 8
+    for j, lv in enumerate(levels):
+        m0 = torch.zeros(D, n8, dtype=torch.int8)
+        m1 = torch.zeros(D, n8, dtype=torch.int8)
+        m0[:, :n] = ge0[:, :, lv].T.to(torch.int8)
+        m1[:, :n] = ge1[:, :, lv].T.to(torch.int8)
+        assert torch.equal(M[0, j].cpu(), m0), j
+        assert torch.equal(M[1, j].cpu(), m1), j
+
+
 @pytest.mark.parametrize("n,D", [(1600, 5120), (301, 1000), (77, 96), (4096, 640), (700, 3900)])
 def test_gram_upper_blocks(n, D):
     """gram_accumulate semantics: two accumulations, rel-max error < 1e-5 vs fp64 (reference
