@@ -33,6 +33,33 @@ import torch
 from . import kernels as KN
 from ._lib import AtlasKernelError, call, dtype_code, load, ptr, stream_ptr
 
+
+class _rf:
+    """Trace range around a hot-path region: always an NVTX range (nsys / ncu `--nvtx`), plus a
+    torch.profiler range while a profiler records. The names are the reference's record_function
+    ranges (atlas.compact, atlas.subsample, atlas.sub.*, atlas.merge.*, atlas.dense; core.py:726-727),
+    so traces of the two builds line up."""
+
+    __slots__ = ("name", "_p")
+
+    def __init__(self, name: str):
+        self.name = name
+        self._p = None
+
+    def __enter__(self):
+        torch.cuda.nvtx.range_push(self.name)
+        if torch.autograd.profiler._is_profiler_enabled:
+            self._p = torch.profiler.record_function(self.name)
+            self._p.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        if self._p is not None:
+            self._p.__exit__(*exc)
+            self._p = None
+        torch.cuda.nvtx.range_pop()
+        return False
+
 NEG_INF = float("-inf")
 I64_MIN = torch.iinfo(torch.int64).min
 M32 = 0xFFFFFFFF
@@ -357,14 +384,16 @@ class Atlas:
         kt = self.kernel_timer
         if not dense:
             cv, cr, cc = self._cand
-            if kt is not None:
-                kt.start("filter")
-            call("atlas_filter_compact", ptr(H), dt, T, D, H.stride(0), ptr(ctx.rowmap32), ptr(self.thr[l, 0]),
-                 ptr(self.thr[l, 1]), ptr(cv[l]), ptr(cr[l]), ptr(cc[l]), ptr(self._counts[l:l + 1]), cap, st)
-            if kt is not None:
-                kt.stop("filter")
+            with _rf("atlas.compact"):
+                if kt is not None:
+                    kt.start("filter")
+                call("atlas_filter_compact", ptr(H), dt, T, D, H.stride(0), ptr(ctx.rowmap32), ptr(self.thr[l, 0]),
+                     ptr(self.thr[l, 1]), ptr(cv[l]), ptr(cr[l]), ptr(cc[l]), ptr(self._counts[l:l + 1]), cap, st)
+                if kt is not None:
+                    kt.stop("filter")
         if self.cfg.subsample and l not in self._sub_done:
-            self._subsample(l, H)
+            with _rf("atlas.subsample"):
+                self._subsample(l, H)
         if self.cfg.reservoir and not dense and ctx.n_r:
             if self._R is None or self._R.shape[1] < ctx.n_r or self._R.dtype != H.dtype:
                 # sized in begin_batch once the activation dtype is known; only the first batch
@@ -372,19 +401,24 @@ class Atlas:
                 assert not self._R_used, "bulk-row buffer resized mid-batch"
                 self._R = torch.empty(self.L, int(ctx.n_r * 1.25) + 1, D, dtype=H.dtype, device=self.dev)
             self._R_used = True
-            KN.gather_rows(H, ctx.res_rows32, self._R[l])
+            with _rf("atlas.merge.bulk"):
+                KN.gather_rows(H, ctx.res_rows32, self._R[l])
         # dense path: forced for dense layers, predicated on count > cap for filtered ones
         (tg, tsc, tt, tv), (rg, rsc, rt, rv) = self._lists
         tcap, rcap = self._list_caps
         c = self.cfg
         fl = self._flags
+        with _rf("atlas.dense"):
+            self._dense_call(H, dt, T, D, l, ctx, c, cap, dense, tg, tsc, tt, tv, tcap, rg, rsc, rt, rv, rcap, fl, st)
+        self._pending[l] = "dense" if dense else "filtered"
+
+    def _dense_call(self, H, dt, T, D, l, ctx, c, cap, dense, tg, tsc, tt, tv, tcap, rg, rsc, rt, rv, rcap, fl, st):
         call("atlas_dense_select", ptr(H), dt, T, D, H.stride(0), l, ptr(ctx.valid32), ctx.n_v, ptr(ctx.tok),
              ptr(ctx.key), ptr(ctx.key_order32), self.B, c.K, c.Kr, int(bool(c.reservoir)), ptr(self.top_seed),
              ptr(self.top_k), ptr(self.res_s), ptr(self.res_seed), ptr(self.E), ptr(self._counts[l:l + 1]), cap,
              int(dense), ptr(tg), ptr(tsc), ptr(tt), ptr(tv), ptr(fl[self.L:self.L + 1]), tcap, ptr(rg), ptr(rsc),
              ptr(rt), ptr(rv), ptr(fl[self.L + 1:self.L + 2]), rcap, ptr(self._dense_scratch),
              self._dense_scratch.numel(), ptr(fl[l:l + 1]), ptr(fl[self.L + 2:self.L + 3]), st)
-        self._pending[l] = "dense" if dense else "filtered"
 
     def _subsample(self, l: int, H: torch.Tensor):
         """Gather the hashed-subsample rows (transposed) and accumulate bin masses, moments,
@@ -420,11 +454,13 @@ class Atlas:
             if self._masks is None or self._masks.numel() < need:
                 self._masks = torch.empty(int(need * 1.25), dtype=torch.int8, device=self.dev)
             masks = self._masks[:need]
-        KN.sub_stats_into(XT, col0, n, self.E[l, 0], self.E[l, 1], levels if ann else [], self.sub_sum[l],
-                          self.sub_sq[l], self.sub_bin[l], masks, n_pad)
+        with _rf("atlas.sub.kernel"):
+            KN.sub_stats_into(XT, col0, n, self.E[l, 0], self.E[l, 1], levels if ann else [], self.sub_sum[l],
+                              self.sub_sq[l], self.sub_bin[l], masks, n_pad)
         if ann:
-            KN.count_gemm_i8(masks.view(2 * len(levels) * D, n_pad), ctx.annT,
-                             self.enr[l].view(2 * len(levels) * D, self.n_a), self.n_a)
+            with _rf("atlas.sub.enrich"):
+                KN.count_gemm_i8(masks.view(2 * len(levels) * D, n_pad), ctx.annT,
+                                 self.enr[l].view(2 * len(levels) * D, self.n_a), self.n_a)
         if self.gram is not None:
             self._stage_fill[l] += n8
             if l == 0:
@@ -436,7 +472,8 @@ class Atlas:
             kt = self.kernel_timer
             if kt is not None:
                 kt.start("gram")
-            KN.gram_upper(self._stage[l], f, self.gram[l])
+            with _rf("atlas.sub.gram"):
+                KN.gram_upper(self._stage[l], f, self.gram[l])
             if kt is not None:
                 kt.stop("gram", work=f)
             self._stage_fill[l] = 0
@@ -463,26 +500,49 @@ class Atlas:
         fl = self._flags
         st = stream_ptr(self.dev)
         cap_main, cap_early = self._cap(ctx, L), self._cap(ctx, 0)
+        with _rf("atlas.merge"):
+            self._merge_batch(ctx, L, c, filt, tg, tsc, tt, tv, rg, rsc, rt, rv, tcap, rcap, fl, st, cap_main,
+                              cap_early)
+        # device-side counters (no sync): compacted survivors of non-overflowed layers, candidates,
+        # overflowed layers (each took one dense pass)
+        self._count_batch(L, c, filt, fl, cap_main, cap_early)
+        self._stats["dense_layer_batches"] += len(dense_done)
+        if not c.naive:
+            self._dense_layers -= set(dense_done)
+        self.n_seen += ctx.n_v
+        self.n_sub += ctx.n_s
+        if self.n_a and ctx.ann_counts is not None:
+            self.ann_tot += ctx.ann_counts
+        self._stats["batches"] += 1
+        self._pending = {}
+        self._active = None
+        return []
+
+    def _merge_batch(self, ctx, L, c, filt, tg, tsc, tt, tv, rg, rsc, rt, rv, tcap, rcap, fl, st, cap_main, cap_early):
+        D, B = self.D, self.B
         if filt:
             mode = (torch.zeros(L, dtype=torch.int8))
             mode[filt] = 1
             cv, cr, cc = self._cand
             R = self._R if (c.reservoir and ctx.n_r) else None
-            call("atlas_admit", L, D, B, c.K, c.Kr, self.U_res, int(bool(c.reservoir)), mode.data_ptr(),
-                 ptr(self._counts), cap_main, cap_early if c.cap_frac_early > 0 else cap_main,
-                 c.early_layers if c.cap_frac_early > 0 else 0, ptr(cv), ptr(cr), ptr(cc), self._cand_cap,
-                 ptr(ctx.tok), ptr(ctx.key), ptr(R), dtype_code(self._act_dtype), ctx.n_r if R is not None else 0,
-                 R.shape[1] if R is not None else 0, ptr(ctx.res_vidx32), ptr(self.top_seed), ptr(self.top_k),
-                 ptr(self.res_s), ptr(self.res_seed), ptr(self.E), ptr(tg), ptr(tsc), ptr(tt), ptr(tv),
-                 ptr(fl[L:L + 1]), tcap, ptr(rg), ptr(rsc), ptr(rt), ptr(rv), ptr(fl[L + 1:L + 2]), rcap,
-                 ptr(fl[L + 2:L + 3]), st)
-        KN.grouped_merge_records(self.top_k, self.top_t, self.top_s, c.K, tg, tsc, tt, tv, fl[L:L + 1], tcap,
-                                 self._ws_top)
+            with _rf("atlas.merge.cand"):
+                call("atlas_admit", L, D, B, c.K, c.Kr, self.U_res, int(bool(c.reservoir)), mode.data_ptr(),
+                     ptr(self._counts), cap_main, cap_early if c.cap_frac_early > 0 else cap_main,
+                     c.early_layers if c.cap_frac_early > 0 else 0, ptr(cv), ptr(cr), ptr(cc), self._cand_cap,
+                     ptr(ctx.tok), ptr(ctx.key), ptr(R), dtype_code(self._act_dtype), ctx.n_r if R is not None else 0,
+                     R.shape[1] if R is not None else 0, ptr(ctx.res_vidx32), ptr(self.top_seed), ptr(self.top_k),
+                     ptr(self.res_s), ptr(self.res_seed), ptr(self.E), ptr(tg), ptr(tsc), ptr(tt), ptr(tv),
+                     ptr(fl[L:L + 1]), tcap, ptr(rg), ptr(rsc), ptr(rt), ptr(rv), ptr(fl[L + 1:L + 2]), rcap,
+                     ptr(fl[L + 2:L + 3]), st)
+        with _rf("atlas.merge.top"):
+            KN.grouped_merge_records(self.top_k, self.top_t, self.top_s, c.K, tg, tsc, tt, tv, fl[L:L + 1], tcap,
+                                     self._ws_top)
         if c.reservoir:
-            KN.grouped_merge_records(self.res_s, self.res_t, self.res_v, c.Kr, rg, rsc, rt, rv, fl[L + 1:L + 2], rcap,
-                                     self._ws_res)
-        # device-side counters (no sync): compacted survivors of non-overflowed layers, candidates,
-        # overflowed layers (each took one dense pass)
+            with _rf("atlas.merge.res"):
+                KN.grouped_merge_records(self.res_s, self.res_t, self.res_v, c.Kr, rg, rsc, rt, rv, fl[L + 1:L + 2],
+                                         rcap, self._ws_res)
+
+    def _count_batch(self, L, c, filt, fl, cap_main, cap_early):
         if filt:
             caps = torch.tensor([cap_early if (c.cap_frac_early > 0 and l < c.early_layers) else cap_main
                                  for l in range(L)], dtype=torch.int32).to(self.dev, non_blocking=True)
@@ -498,17 +558,6 @@ class Atlas:
             upd = torch.stack([torch.zeros((), dtype=torch.int64, device=self.dev), fl[L].to(torch.int64),
                                fl[L + 1].to(torch.int64), torch.zeros((), dtype=torch.int64, device=self.dev)])
         self._dev_stats += upd
-        self._stats["dense_layer_batches"] += len(dense_done)
-        if not c.naive:
-            self._dense_layers -= set(dense_done)
-        self.n_seen += ctx.n_v
-        self.n_sub += ctx.n_s
-        if self.n_a and ctx.ann_counts is not None:
-            self.ann_tot += ctx.ann_counts
-        self._stats["batches"] += 1
-        self._pending = {}
-        self._active = None
-        return []
 
     def check_errors(self):
         """Raise if a device-side list ran out of capacity (never expected: lists are sized for the

@@ -45,9 +45,49 @@ def atomic_save(obj, path: Path):
     os.replace(tmp, path)
 
 
-def latest_ckpt(d: Path):
+def write_profile(prof, path: Path, dev):
+    """Kernel table (key_averages, by device time) plus the per-range attribution of the Chrome
+    trace (span / busy / idle per atlas.* range with its top kernels) and the gzipped trace, as
+    the reference's --profile-at output (run_atlas.py:341-365)."""
+    import gzip
+    import shutil
+    from .proftrace import attribute, table
+    try:
+        tp = path.with_suffix(".trace.json")
+        prof.export_chrome_trace(str(tp))
+        res = attribute(tp)
+        path.with_name(path.stem + "_ranges.txt").write_text(table(res, top=10))
+        path.with_name(path.stem + "_ranges.json").write_text(json.dumps(res))
+        with open(tp, "rb") as fi, gzip.open(str(tp) + ".gz", "wb") as fo:
+            shutil.copyfileobj(fi, fo)
+        tp.unlink()
+    except Exception as e:  # noqa: BLE001  the attribution is a diagnostic; the run goes on
+        print(f"[atlas] trace attribution failed: {e!r}", flush=True)
+    ka = prof.key_averages()
+    keys = ("self_device_time_total", "self_cuda_time_total") if torch.device(dev).type == "cuda" else ("self_cpu_time_total",)
+    for key in keys:
+        try:
+            path.write_text(ka.table(sort_by=key, row_limit=60))
+            return
+        except Exception:  # noqa: BLE001  key names differ between torch versions
+            continue
+    path.write_text(ka.table(row_limit=60))
+
+
+def load_latest_ckpt(d: Path):
+    """(path, checkpoint dict) of the newest readable checkpoint in d, or (None, None). A newest file
+    that cannot be read (truncated by a kill during a copy, or damaged) is reported and skipped in
+    favour of the one before it: the writer keeps the last two (atomic tmp + fsync + rename)."""
     c = sorted(d.glob("ckpt_*.pt"), key=lambda p: int(p.stem.split("_")[1]))
-    return c[-1] if c else None
+    for p in reversed(c):
+        try:
+            st = torch.load(p, weights_only=False, map_location="cpu")
+            if not isinstance(st, dict) or "atlas" not in st or "next_batch" not in st:
+                raise ValueError("not an atlas checkpoint")
+            return p, st
+        except Exception as e:  # noqa: BLE001  any unreadable file: fall back to the previous one
+            print(f"[atlas] skipping unreadable checkpoint {p.name}: {type(e).__name__}: {e}", flush=True)
+    return None, None
 
 
 def parser():
@@ -183,11 +223,10 @@ def main(argv=None):
     cfg = AtlasConfig(K=a.K, Kr=a.Kr, backend=a.backend, seed=a.seed, reservoir=not a.no_reservoir,
                       subsample=not a.no_subsample, gram=not a.no_gram and not a.no_subsample, naive=a.naive,
                       stats_impl=a.stats_impl, merge_impl=a.merge_impl, cap_frac_early=a.cap_frac_early)
-    ck = latest_ckpt(ck_dir) if a.resume else None
+    ck, st = load_latest_ckpt(ck_dir) if a.resume else (None, None)
     t1 = time.time()
     seeds = None
     if ck is not None:
-        st = torch.load(ck, weights_only=False)
         assert st["args_key"] == _args_key(a), "resume with different run arguments"
         E = st["atlas"]["E"]
         start = st["next_batch"]
@@ -266,6 +305,13 @@ def main(argv=None):
                 sync(dev)
                 fwd_s = time.time() - tf0
                 atlas.enabled = True
+            prof = None
+            if bi in a.profile_at:
+                acts = [torch.profiler.ProfilerActivity.CPU]
+                if torch.device(dev).type == "cuda":
+                    acts.append(torch.profiler.ProfilerActivity.CUDA)
+                prof = torch.profiler.profile(activities=acts)
+                prof.__enter__()
             ta0 = time.time()
             ctx = ctx_host.to(dev) if ctx_host is not None else atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann)
             n_before = atlas.n_seen
@@ -278,6 +324,10 @@ def main(argv=None):
                 atlas.flush_gram()
             sync(dev)
             atlas_s = time.time() - ta0
+            if prof is not None:
+                prof.__exit__(None, None, None)
+                write_profile(prof, out / f"profile_batch_{bi}.txt", dev)
+                log(f"[atlas] profiled batch {bi} -> profile_batch_{bi}.txt")
             rec = {"batch": bi, "n_seen_before": n_before, "n_valid": ctx.n_v, "rows": b.n_rows,
                    "Lmax": int(b.input_ids.shape[1]), "seconds": time.time() - tb, "t_start": tb, "t_end": time.time(),
                    "fwd_only_s": fwd_s, "atlas_pass_s": atlas_s,

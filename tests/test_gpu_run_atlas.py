@@ -42,3 +42,18 @@ def test_full_run_equals_stop_and_resume(tmp_path, seeded):
     assert torch.allclose(A["sub_sum"], B["sub_sum"], rtol=1e-9, atol=1e-9)
     assert A["n_seen"] == B["n_seen"] and A["n_sub"] == B["n_sub"]
     assert B["gram_rows"] < A["gram_rows"]  # the resumed run's Gram covers the batches after the resume
+
+
+def test_profile_at_writes_kernel_table_and_range_attribution(tmp_path):
+    """--profile-at (run_atlas.py:240-266 of the reference): the profiled batch gets a kernel table,
+    a per-range attribution in which the atlas ranges own the atlas kernels, and the trace."""
+    out = tmp_path / "prof"
+    _run(["--model", "8M", "--data", "synthetic:200:3", "--device", "cuda:0", "--dtype", "bf16",
+          "--tokens-per-batch", "8192", "--pilot-tokens", "8192", "--K", "16", "--Kr", "8", "--seed-thresholds",
+          "--profile-at", "2", "--out", str(out)], ROOT)
+    assert (out / "profile_batch_2.txt").stat().st_size > 0
+    assert (out / "profile_batch_2.trace.json.gz").exists()
+    import json
+    res = json.loads((out / "profile_batch_2_ranges.json").read_text())
+    assert "filter_bulk_kernel" in " ".join(res["atlas.compact"]["kernels"])
+    assert res["atlas.merge.top"]["busy_us"] > 0
