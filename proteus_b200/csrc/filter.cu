@@ -473,13 +473,49 @@ constexpr int kBCtasPerSm = ATLAS_FILTER_BCTAS;
 constexpr int kBSeg = 512;                       // bytes of one row segment (256 bf16 columns)
 constexpr int kBStage = 1024;                    // staged survivors per CTA (12 KB)
 
+#ifndef ATLAS_FILTER_QUEUE
+#define ATLAS_FILTER_QUEUE 1
+#endif
+constexpr int kBQueue = 64;  // flagged row vectors parked per consumer warp
+
+// Flagged row vectors of one consumer warp, waiting for extraction: the 16 bytes, the row-map entry
+// and the lane (the lane gives the 8 columns and their thresholds).
+struct HitQueue {
+  uint4 x[kBQueue];
+  int32_t v[kBQueue];
+  int32_t lane[kBQueue];
+};
+
 struct BulkSmem {
   uint4 data[kBStages][kBRows][kBSeg / 16];
   int32_t rows[kBStages][kBRows];
   uint64_t full[kBStages], empty[kBStages];
   StageAreaN<kBStage> sa;
+  uint4 thr[32][2];  // per lane of the strip: bf16x2 thresholds (positive, negative pole)
+  HitQueue q[kBWarps];
   int s_base;
 };
+
+// Extraction of a warp's parked row vectors: lane i takes entries i, i+32, ..., each with one
+// staging reservation (no divergence beyond the per-entry survivor count).
+template <class SA>
+__device__ __forceinline__ void drain_queue(const HitQueue& q, int qn, const uint4 (&thr)[32][2], int s0, int lane, SA& sa,
+                                            float* __restrict__ out_val, int32_t* __restrict__ out_row,
+                                            int32_t* __restrict__ out_col, int32_t* __restrict__ count, int64_t cap) {
+  __syncwarp();
+  for (int e = lane; e < qn; e += 32) {
+    const uint4 xe[1] = {q.x[e]};
+    const int32_t ve[1] = {q.v[e]};
+    const int L = q.lane[e];
+    const uint4 tw = thr[L][0], nw = thr[L][1];
+    const __nv_bfloat162 tp2[4] = {*reinterpret_cast<const __nv_bfloat162*>(&tw.x), *reinterpret_cast<const __nv_bfloat162*>(&tw.y),
+                                   *reinterpret_cast<const __nv_bfloat162*>(&tw.z), *reinterpret_cast<const __nv_bfloat162*>(&tw.w)};
+    const __nv_bfloat162 tn2[4] = {*reinterpret_cast<const __nv_bfloat162*>(&nw.x), *reinterpret_cast<const __nv_bfloat162*>(&nw.y),
+                                   *reinterpret_cast<const __nv_bfloat162*>(&nw.z), *reinterpret_cast<const __nv_bfloat162*>(&nw.w)};
+    bf16_emit_step<1>(1u, xe, ve, tp2, tn2, s0 + L * 8, sa, out_val, out_row, out_col, count, cap);
+  }
+  __syncwarp();
+}
 
 __global__ void __launch_bounds__(kBThreads, kBCtasPerSm)
 filter_bulk_kernel(const __grid_constant__ CUtensorMap tmap, int T, int D, int rows_per_cta,
@@ -555,6 +591,19 @@ filter_bulk_kernel(const __grid_constant__ CUtensorMap tmap, int T, int D, int r
       tn2[w] = __halves2bfloat162(n[0], n[1]);
     }
     constexpr int U = kBRows / kBWarps;
+#if ATLAS_FILTER_QUEUE
+    // Survivors are rare: a lane with hits parks its flagged row vectors in the warp's queue
+    // (positions from ballots, no atomics) and the warp extracts them 32 at a time, all lanes
+    // busy, instead of the whole warp idling through one lane's extraction.
+    if (warp == 0) {
+      sm.thr[lane][0] = *reinterpret_cast<const uint4*>(tp2);
+      sm.thr[lane][1] = *reinterpret_cast<const uint4*>(tn2);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kBWarps * 32) : "memory");  // consumer warps only
+    HitQueue& q = sm.q[warp];
+    const uint32_t lt = (1u << lane) - 1u;
+    int qn = 0;  // warp-uniform fill of the queue
+#endif
     for (int k = 0; k < n_stages; ++k) {
       const int st = k % kBStages;
       if (!__all_sync(0xFFFFFFFFu, tc::mbar_wait(&sm.full[st], (uint32_t)(k / kBStages) & 1, 303))) break;
@@ -569,8 +618,47 @@ filter_bulk_kernel(const __grid_constant__ CUtensorMap tmap, int T, int D, int r
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&sm.empty[st]);
       const uint32_t flags = bf16_flags<U>(x, v, tp2, tn2);
+#if ATLAS_FILTER_QUEUE
+      uint32_t bal[U];
+      int tot = 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        bal[u] = __ballot_sync(0xFFFFFFFFu, (flags >> u) & 1u);
+        tot += __popc(bal[u]);
+      }
+      if (tot) {
+        if (tot > kBQueue) {  // denser than the queue: extract in place
+          if (flags) bf16_emit_step<U>(flags, x, v, tp2, tn2, c0, sm.sa, out_val, out_row, out_col, count, cap);
+        } else {
+          if (qn + tot > kBQueue) {
+            drain_queue(q, qn, sm.thr, s0, lane, sm.sa, out_val, out_row, out_col, count, cap);
+            qn = 0;
+          }
+          int base = qn;
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            if ((flags >> u) & 1u) {
+              const int pos = base + __popc(bal[u] & lt);
+              q.x[pos] = x[u];
+              q.v[pos] = v[u];
+              q.lane[pos] = lane;
+            }
+            base += __popc(bal[u]);
+          }
+          qn += tot;
+          if (qn >= 32) {
+            drain_queue(q, qn, sm.thr, s0, lane, sm.sa, out_val, out_row, out_col, count, cap);
+            qn = 0;
+          }
+        }
+      }
+#else
       if (flags) bf16_emit_step<U>(flags, x, v, tp2, tn2, c0, sm.sa, out_val, out_row, out_col, count, cap);
+#endif
     }
+#if ATLAS_FILTER_QUEUE
+    if (qn) drain_queue(q, qn, sm.thr, s0, lane, sm.sa, out_val, out_row, out_col, count, cap);
+#endif
   }
   __syncthreads();
   const int staged_n = sm.sa.n < kBStage ? sm.sa.n : kBStage;  // slots [0, staged_n) are all staged
