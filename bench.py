@@ -36,9 +36,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 # DRAM bytes (read + write) per row of H of one filter launch, from the ncu capture of the C2 case
-# (dram__bytes_read.sum + dram__bytes_write.sum = 167.92 MB + 5.62 MB over 16384 rows of 5120 bf16
+# (dram__bytes_read.sum + dram__bytes_write.sum = 167.91 MB + 3.83 MB over 16384 rows of 5120 bf16
 # columns at 0.3% survivors); the filter's traffic grows with the rows it streams.
-FILTER_DRAM_BYTES_PER_ROW = (167.919872e6 + 5.618176e6) / 16384
+FILTER_DRAM_BYTES_PER_ROW = (167.91424e6 + 3.827712e6) / 16384
 METRIC = "ESM-2 650M atlas tokens/s"
 L_650M, D_650M = 33, 5120
 
