@@ -176,6 +176,58 @@ sub_stats_kernel(const typename Elem<DT>::T* __restrict__ XT, int64_t ldx, int64
   }
 }
 
+// One 8-row vector of one column (bf16 path below): fp32 sums of the vector folded into the fp64
+// totals, cumulative edge counts from the compare masks (16 bits per counted row), and the int8
+// level masks (one byte per row, rows i..i+7 little-endian in one 8-byte store per plane). kFull:
+// every row of the vector is < n (no validity mask).
+template <bool kFull>
+__device__ __forceinline__ void stats_vec8(const uint32_t (&w4)[4], const uint32_t (&vm)[4], const __nv_bfloat162 (&pe)[kMaxB],
+                                           const __nv_bfloat162 (&ne)[kMaxB], const uint32_t (&levmask)[kMaxB], int B,
+                                           int NL, int (&c0)[kMaxB], int (&c1)[kMaxB], double& acc_s, double& acc_q,
+                                           int8_t* __restrict__ mrow, int64_t plane) {
+  float s32 = 0.0f, q32 = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float lo = __uint_as_float(w4[w] << 16), hi = __uint_as_float(w4[w] & 0xFFFF0000u);
+    s32 += lo;
+    s32 += hi;
+    q32 = fmaf(lo, lo, q32);
+    q32 = fmaf(hi, hi, q32);
+  }
+  acc_s += (double)s32;
+  acc_q += (double)q32;
+#pragma unroll
+  for (int b = 0; b < kMaxB; ++b) {
+    if (b >= B) break;
+    uint32_t mp[4], mn[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
+      mp[w] = __hge2_mask(h2, pe[b]);
+      mn[w] = __hle2_mask(h2, ne[b]);
+      if (!kFull) {
+        mp[w] &= vm[w];
+        mn[w] &= vm[w];
+      }
+    }
+    c0[b] += __popc(mp[0]) + __popc(mp[1]) + __popc(mp[2]) + __popc(mp[3]);
+    c1[b] += __popc(mn[0]) + __popc(mn[1]) + __popc(mn[2]) + __popc(mn[3]);
+    uint32_t lm = mrow ? levmask[b] : 0u;
+    if (lm) {
+      const uint64_t wp = (uint64_t)(__byte_perm(mp[0], mp[1], 0x6420) & 0x01010101u) |
+                          ((uint64_t)(__byte_perm(mp[2], mp[3], 0x6420) & 0x01010101u) << 32);
+      const uint64_t wn = (uint64_t)(__byte_perm(mn[0], mn[1], 0x6420) & 0x01010101u) |
+                          ((uint64_t)(__byte_perm(mn[2], mn[3], 0x6420) & 0x01010101u) << 32);
+      while (lm) {
+        const int j = __ffs(lm) - 1;
+        lm &= lm - 1;
+        *reinterpret_cast<uint64_t*>(mrow + (int64_t)j * plane) = wp;
+        *reinterpret_cast<uint64_t*>(mrow + (int64_t)(NL + j) * plane) = wn;
+      }
+    }
+  }
+}
+
 // bf16 path of the same statistics, on packed pairs: every edge compare is one bf16x2 compare per
 // two rows against the edge rounded to bf16 (up for the positive pole x >= E0; down for the
 // negative pole, x <= -E1), which for bf16 values is exactly the fp32 compare: no bf16 lies
@@ -209,60 +261,26 @@ sub_stats_bf16_kernel(const __nv_bfloat16* __restrict__ XT, int64_t ldx, int64_t
   double acc_s = 0.0, acc_q = 0.0;
   const __nv_bfloat16* col = XT + d * ldx + col0;
   const int64_t n_loop = masks ? n_pad : n;
-  for (int64_t i = (int64_t)lane * 8; i < n_loop; i += 256) {
+  const int64_t plane = D * n_pad;  // bytes between mask planes (pole, level)
+  int64_t i = (int64_t)lane * 8;
+  for (; i + 8 <= n; i += 256) {  // whole 8-row vectors: no row is masked
+    const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(col + i));
+    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+    stats_vec8<true>(w4, w4, pe, ne, levmask, B, NL, c0, c1, acc_s, acc_q, masks ? masks + d * n_pad + i : nullptr,
+                     plane);
+  }
+  for (; i < n_loop; i += 256) {  // the ragged end of the column (and mask padding past n): rows >= n are zero, uncounted
+    const unsigned short* c16 = reinterpret_cast<const unsigned short*>(col);
     uint32_t w4[4], vm[4];
-    if (i + 8 <= n) {
-      const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(col + i));
-      w4[0] = raw.x; w4[1] = raw.y; w4[2] = raw.z; w4[3] = raw.w;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) vm[w] = 0xFFFFFFFFu;
-    } else {  // the ragged end of the column (and mask padding past n): rows >= n are zero, uncounted
-      const unsigned short* c16 = reinterpret_cast<const unsigned short*>(col);
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const int64_t r = i + 2 * w;
-        const uint32_t lo = r < n ? c16[r] : 0u, hi = r + 1 < n ? c16[r + 1] : 0u;
-        w4[w] = lo | (hi << 16);
-        vm[w] = (r < n ? 0x0000FFFFu : 0u) | (r + 1 < n ? 0xFFFF0000u : 0u);
-      }
-    }
-    float s32 = 0.0f, q32 = 0.0f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float lo = __uint_as_float(w4[w] << 16), hi = __uint_as_float(w4[w] & 0xFFFF0000u);
-      s32 += lo;
-      s32 += hi;
-      q32 = fmaf(lo, lo, q32);
-      q32 = fmaf(hi, hi, q32);
+      const int64_t r = i + 2 * w;
+      const uint32_t lo = r < n ? c16[r] : 0u, hi = r + 1 < n ? c16[r + 1] : 0u;
+      w4[w] = lo | (hi << 16);
+      vm[w] = (r < n ? 0x0000FFFFu : 0u) | (r + 1 < n ? 0xFFFF0000u : 0u);
     }
-    acc_s += (double)s32;
-    acc_q += (double)q32;
-#pragma unroll
-    for (int b = 0; b < kMaxB; ++b) {
-      if (b >= B) break;
-      uint32_t mp[4], mn[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
-        mp[w] = __hge2_mask(h2, pe[b]) & vm[w];
-        mn[w] = __hle2_mask(h2, ne[b]) & vm[w];
-      }
-      c0[b] += __popc(mp[0]) + __popc(mp[1]) + __popc(mp[2]) + __popc(mp[3]);
-      c1[b] += __popc(mn[0]) + __popc(mn[1]) + __popc(mn[2]) + __popc(mn[3]);
-      uint32_t lm = masks ? levmask[b] : 0u;
-      if (lm) {  // one byte (0/1) per row, rows i..i+7 little-endian in one 8-byte store
-        const uint64_t wp = (uint64_t)(__byte_perm(mp[0], mp[1], 0x6420) & 0x01010101u) |
-                            ((uint64_t)(__byte_perm(mp[2], mp[3], 0x6420) & 0x01010101u) << 32);
-        const uint64_t wn = (uint64_t)(__byte_perm(mn[0], mn[1], 0x6420) & 0x01010101u) |
-                            ((uint64_t)(__byte_perm(mn[2], mn[3], 0x6420) & 0x01010101u) << 32);
-        while (lm) {
-          const int j = __ffs(lm) - 1;
-          lm &= lm - 1;
-          *reinterpret_cast<uint64_t*>(masks + ((int64_t)(0 * NL + j) * D + d) * n_pad + i) = wp;
-          *reinterpret_cast<uint64_t*>(masks + ((int64_t)(1 * NL + j) * D + d) * n_pad + i) = wn;
-        }
-      }
-    }
+    stats_vec8<false>(w4, vm, pe, ne, levmask, B, NL, c0, c1, acc_s, acc_q, masks ? masks + d * n_pad + i : nullptr,
+                      plane);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

@@ -70,6 +70,34 @@ def test_filter_large_vector_path():
     assert torch.equal(v[:n], Hf[inv[r[:n]], c[:n]])
 
 
+def test_filter_density_mix_partial_strip():
+    """TMA-fed bf16 path: ragged T, a partial last strip (D = 1000 = 3 x 256 + 232 columns), padding
+    rows, and columns from near-dense (most values survive: more flagged rows per warp step than the
+    hit queue holds) to sparse, against the fp32 comparison; plus the exact count past a small cap."""
+    KN = _kn()
+    g = torch.Generator(device=DEV).manual_seed(11)
+    T, D = 1333, 1000
+    H = torch.randn(T, D, generator=g, device=DEV).to(torch.bfloat16)
+    valid = torch.rand(T, generator=g, device=DEV) > 0.07
+    rowmap = torch.full((T,), -1, dtype=torch.int64, device=DEV)
+    rowmap[valid] = torch.arange(int(valid.sum()), device=DEV)
+    level = torch.rand(D, generator=g, device=DEV)
+    tp = torch.where(level < 0.1, torch.full_like(level, -2.0), 1.5 + 2.0 * level)  # 10% near-dense columns
+    tn = torch.where(level > 0.95, torch.full_like(level, -2.0), 1.5 + 2.0 * (1 - level))
+    v, r, c, cnt = KN.filter_candidates(H, rowmap, tp, tn, 1 << 21)
+    n = int(cnt)
+    Hf = H.float()
+    mask = ((Hf > tp) | (-Hf > tn)) & valid[:, None]
+    rt, ct = torch.nonzero(mask, as_tuple=True)
+    assert n == rt.numel()
+    key = lambda a, b: (a * D + b).sort().values  # noqa: E731
+    assert torch.equal(key(r[:n], c[:n]), key(rowmap[rt], ct))
+    inv = torch.nonzero(valid).squeeze(1)
+    assert torch.equal(v[:n], Hf[inv[r[:n]], c[:n]])
+    _, _, _, cnt_small = KN.filter_candidates(H, rowmap, tp, tn, 1000)
+    assert int(cnt_small) == n
+
+
 def test_filter_bf16_threshold_edges():
     """bf16 path compares packed bf16 pairs against bf16-rounded thresholds; the survivors must be
     those of the fp32 comparison for thresholds equal to a bf16 value (ties do not survive),
