@@ -618,7 +618,8 @@ def main():
     atlas.check_errors()
     combine_ms = None
     if world > 1:  # exact cross-GPU combine of the shard states (not part of the per-step metric)
-        from proteus_b200.dist import merge_states
+        from proteus_b200.dist import merge_states, warm_up
+        warm_up(device=dev)  # peer connections of the exchange are set up outside the timed combine
         barrier(world, local)
         torch.cuda.synchronize()
         a4, b4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

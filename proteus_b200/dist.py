@@ -72,6 +72,24 @@ def _sum_in_rank_order(t: torch.Tensor, world, group) -> torch.Tensor:
     return acc
 
 
+def warm_up(group=None, device=None):
+    """Run each collective of merge_states once on a few bytes. The backend sets up its peer
+    connections (NCCL: one channel per peer for the all-to-all) on first use; doing it here keeps
+    that one-time cost out of a timed combine. Every rank must call it."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return
+    dev = device if device is not None else torch.device("cpu")
+    w = torch.zeros(world * 8, dtype=torch.int64, device=dev)
+    dist.all_to_all_single(torch.empty_like(w), w, group=group)
+    dist.all_gather_into_tensor(torch.empty_like(w), w[:8].contiguous(), group=group)
+    bufs = [torch.empty(8, dtype=torch.int64, device=dev) for _ in range(world)]
+    dist.all_gather(bufs, w[:8].contiguous(), group=group)
+    dist.all_reduce(w[:1], op=dist.ReduceOp.SUM, group=group)
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+
+
 @torch.no_grad()
 def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
     """Combine the shard atlases of all ranks in place; afterwards every rank holds the merged

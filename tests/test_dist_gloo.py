@@ -57,11 +57,12 @@ def _worker(rank, world, port, mode, q):
         import datetime
         torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
                                              timeout=datetime.timedelta(seconds=20))
-        from proteus_b200.dist import merge_states, shard_plan
+        from proteus_b200.dist import merge_states, shard_plan, warm_up
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure before the combine")
         z = golden("merge_from")
         a = _shard(z, rank)
+        warm_up()
         merge_states(a, row_merge=cpu_row_merge, gram=False)
         want = {k[2:]: v for k, v in z.items() if k.startswith("m_")}
         L, D, K, B, Kr = 2, 48, 8, 5, 4
