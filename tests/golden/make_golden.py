@@ -18,8 +18,9 @@ seeded inputs and stores every result field in compressed .npz files next to thi
   c1_esm8m.npz        BASELINE config 0: ESM-2 8M random-init fp32 CPU forward feeding the
                       reference Atlas (stats v1, merge loop), pilot edges + seeds from 64 sequences
 
-Usage (in the build container, where the reference is mounted):
-  python tests/golden/make_golden.py --ref /root/reference [--only c1]
+Usage (with a read-only checkout of the reference project; the path may also come from
+the PROTEUS_REF environment variable):
+  python tests/golden/make_golden.py --ref <path to the haelyons/proteus checkout> [--only c1]
 """
 from __future__ import annotations
 
@@ -322,7 +323,8 @@ def compact_exact_fields(path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("PROTEUS_REF"), required=os.environ.get("PROTEUS_REF") is None,
+                    help="checkout of the reference project (read-only)")
     ap.add_argument("--only", nargs="*", default=None)
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
