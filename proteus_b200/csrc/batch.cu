@@ -53,6 +53,40 @@ __global__ void gather_transpose_kernel(const T* __restrict__ H, int64_t D, int6
   }
 }
 
+// 2-byte types with 16-byte-aligned rows: 64 (rows i) x 64 (columns d) tiles; each thread loads
+// two 16-byte vectors (8 columns of one row, coalesced along the row) and stores two 16-byte
+// vectors of XT (8 consecutive rows of one column). Shared-memory reads walk the tile with the
+// column index fastest, so a warp reads one tile row (no bank conflicts). Rows >= n are zeros.
+__global__ void __launch_bounds__(256)
+gather_transpose16_kernel(const uint16_t* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
+                          int64_t n, int64_t n8, uint16_t* __restrict__ XT, int64_t ldx, int64_t col0) {
+  __shared__ __align__(16) uint16_t tile[64][64];
+  const int64_t i0 = (int64_t)blockIdx.x * 64, d0 = (int64_t)blockIdx.y * 64;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int c = threadIdx.x + 256 * j;
+    const int r = c >> 3, ch = c & 7;
+    const int64_t i = i0 + r, d = d0 + ch * 8;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (i < n && d < D) v = __ldg(reinterpret_cast<const uint4*>(H + (int64_t)rows[i] * ld + d));
+    *reinterpret_cast<uint4*>(&tile[r][ch * 8]) = v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int c = threadIdx.x + 256 * j;
+    const int dd = c & 63, ch = c >> 6;
+    const int64_t d = d0 + dd, i = i0 + ch * 8;
+    if (d < D && i < n8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        w[k] = (uint32_t)tile[ch * 8 + 2 * k][dd] | ((uint32_t)tile[ch * 8 + 2 * k + 1][dd] << 16);
+      *reinterpret_cast<uint4*>(XT + d * ldx + col0 + i) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
 template <typename T>
 __global__ void gather_rows_kernel(const T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
                                    int64_t n, T* __restrict__ R) {
@@ -355,6 +389,13 @@ extern "C" int atlas_gather_transpose(const void* H, int dtype, int64_t T, int64
   ATLAS_REQUIRE(grid.y < 65536, "gather_transpose: D too large");
   dim3 block(32, 8);
   cudaStream_t st = (cudaStream_t)stream;
+  if ((dtype == ATLAS_BF16 || dtype == ATLAS_F16) && D % 8 == 0 && ld % 8 == 0 && ldx % 8 == 0 && col0 % 8 == 0 &&
+      (uintptr_t)H % 16 == 0 && (uintptr_t)XT % 16 == 0) {
+    dim3 g16((unsigned)((n8 + 63) / 64), (unsigned)((D + 63) / 64));
+    ATLAS_REQUIRE(g16.y < 65536, "gather_transpose: D too large");
+    gather_transpose16_kernel<<<g16, 256, 0, st>>>((const uint16_t*)H, D, ld, rows, n, n8, (uint16_t*)XT, ldx, col0);
+    return check_launch("atlas_gather_transpose");
+  }
   switch (dtype) {
     case ATLAS_BF16:
       gather_transpose_kernel<__nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)H, D, ld, rows, n, n8,
