@@ -214,7 +214,11 @@ class Atlas:
             self.enr = torch.zeros(L, 2, nl, D, n_annot, dtype=torch.int64, device=dev)
             self.ann_tot = torch.zeros(n_annot, dtype=torch.int64, device=dev)
         self.gram = torch.zeros(L, D, D, dtype=torch.float32, device=dev) if cfg.gram else None
-        self.gram64 = torch.zeros(L, D, D, dtype=torch.float64) if cfg.gram else None
+        # fp64 Gram accumulator: on the device by default (a flush is then one device add instead of a
+        # 4 B/element copy to the host and a host add; 2x the fp32 Gram in HBM, e.g. 6.9 GB for
+        # 33 x 5120^2); PROTEUS_GRAM64_HOST=1 keeps it in host memory as the reference does.
+        g64_dev = "cpu" if os.environ.get("PROTEUS_GRAM64_HOST", "0") == "1" else dev
+        self.gram64 = torch.zeros(L, D, D, dtype=torch.float64, device=g64_dev) if cfg.gram else None
         self.gram_rows = 0
         self.top_seed = torch.full((G,), NEG_INF, device=dev)
         self.res_seed = torch.full((G * B,), I64_MIN, dtype=torch.long, device=dev)
@@ -567,10 +571,10 @@ class Atlas:
 
     # ------------------------------------------------------------------ outputs
     def flush_gram(self):
-        """fp32 device Gram (after draining staged rows) -> fp64 host accumulator (core.py:593-599)."""
+        """fp32 device Gram (after draining staged rows) -> fp64 accumulator (core.py:593-599)."""
         if self.gram is not None:
             self._drain_gram()
-            self.gram64 += self.gram.cpu().double()
+            self.gram64 += self.gram.to(self.gram64.device).double()
             self.gram.zero_()
 
     _STATE = ["top_s", "top_t", "top_k", "res_s", "res_t", "res_v", "sub_sum", "sub_sq", "sub_bin", "E",
@@ -621,7 +625,7 @@ class Atlas:
         if self.gram is not None:
             self.flush_gram()
             other.flush_gram()
-            self.gram64 += other.gram64
+            self.gram64 += other.gram64.to(self.gram64.device)
             self.gram_rows += other.gram_rows
         self.n_seen += other.n_seen
         self.n_sub += other.n_sub
@@ -648,7 +652,7 @@ class Atlas:
             out["enr"] = self.enr.cpu()
             out["ann_tot"] = self.ann_tot.cpu()
         if self.gram is not None:
-            out["gram"] = symmetrize_upper(self.gram64)
+            out["gram"] = symmetrize_upper(self.gram64.cpu())
             out["gram_rows"] = self.gram_rows
         out.update(self.verify_seeds())
         return out

@@ -125,7 +125,7 @@ def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
         atlas.flush_gram()
         for l in range(atlas.gram64.shape[0]):
             g = atlas.gram64[l].to(dev)
-            atlas.gram64[l].copy_(_sum_in_rank_order(g, world, group).cpu())
+            atlas.gram64[l].copy_(_sum_in_rank_order(g, world, group).to(atlas.gram64.device))
         atlas.gram_rows = int(cnt[2])
     stats = [None] * world
     dist.all_gather_object(stats, dict(atlas.stats), group=group)

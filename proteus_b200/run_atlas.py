@@ -74,6 +74,43 @@ def write_profile(prof, path: Path, dev):
     path.write_text(ka.table(row_limit=60))
 
 
+class CheckpointWriter:
+    """Checkpoints written behind the stream. `save` takes a host copy of the state on the calling
+    thread (a consistent snapshot between two batches; the device keeps working on the next batch
+    afterwards) and hands the disk write (tmp + fsync + rename), the pruning to the newest `keep`
+    files and an optional follow-up (the run summary) to a background thread, so a multi-GB
+    checkpoint no longer stalls the batch loop. One write is in flight at a time: a new checkpoint
+    first waits for the previous one. `wait` joins the write and re-raises its error, if any."""
+
+    def __init__(self, ck_dir: Path, keep: int = 2):
+        self.ck_dir, self.keep = ck_dir, keep
+        self._t = None
+        self._err = None
+
+    def _write(self, obj, path: Path, after):
+        try:
+            atomic_save(obj, path)
+            for old in sorted(self.ck_dir.glob("ckpt_*.pt"), key=lambda q: int(q.stem.split("_")[1]))[:-self.keep]:
+                old.unlink()
+            if after is not None:
+                after()
+        except BaseException as e:  # noqa: BLE001  re-raised on the caller's thread by wait()
+            self._err = e
+
+    def save(self, obj, path: Path, after=None):
+        self.wait()
+        self._t = threading.Thread(target=self._write, args=(obj, path, after), name="ckpt-writer")
+        self._t.start()
+
+    def wait(self):
+        if self._t is not None:
+            self._t.join()
+            self._t = None
+        if self._err is not None:
+            e, self._err = self._err, None
+            raise e
+
+
 def load_latest_ckpt(d: Path):
     """(path, checkpoint dict) of the newest readable checkpoint in d, or (None, None). A newest file
     that cannot be read (truncated by a kill during a copy, or damaged) is reported and skipped in
@@ -271,18 +308,22 @@ def main(argv=None):
     logf = open(out / ("batches.jsonl" if world == 1 else f"batches.rank{rank}.jsonl"), "a")
     ckpt_s, batch_s, last_ckpt_s = 0.0, 0.0, None
 
+    writer = CheckpointWriter(ck_dir, keep=2)
+
     def save_ckpt(next_batch):
+        """Snapshot now, write in the background; the time on the batch loop's path is the host copy
+        (plus any wait for the previous write)."""
         nonlocal ckpt_s, last_ckpt_s
         t = time.time()
-        atomic_save({"atlas": atlas.state_dict(), "next_batch": next_batch, "args_key": _args_key(a), "model": info},
-                    ck_dir / f"ckpt_{next_batch}.pt")
-        for old in sorted(ck_dir.glob("ckpt_*.pt"), key=lambda p: int(p.stem.split("_")[1]))[:-2]:
-            old.unlink()
+        obj = {"atlas": atlas.state_dict(), "next_batch": next_batch, "args_key": _args_key(a), "model": info}
+        after = None
         if rank == 0:
-            (out / "run.json").write_text(json.dumps(summary(False, next_batch), indent=1))
+            sm = summary(False, next_batch)
+            after = lambda: (out / "run.json").write_text(json.dumps(sm, indent=1))  # noqa: E731
+        writer.save(obj, ck_dir / f"ckpt_{next_batch}.pt", after)
         last_ckpt_s = time.time() - t
         ckpt_s = max(ckpt_s, last_ckpt_s)
-        log(f"[atlas] checkpoint at batch {next_batch}/{len(my_plan)} ({last_ckpt_s:.1f}s)")
+        log(f"[atlas] checkpoint at batch {next_batch}/{len(my_plan)} ({last_ckpt_s:.1f}s on the loop, written in the background)")
 
     t2 = time.time()
     n_done = 0
@@ -344,13 +385,16 @@ def main(argv=None):
             if a.deadline and bi + 1 < len(my_plan) and time.time() > a.deadline - 2 * (batch_s + max(ckpt_s, 30.0)):
                 if (bi + 1) % a.ckpt_every:
                     save_ckpt(bi + 1)
+                writer.wait()
                 log(f"[atlas] deadline approaching: stopped cleanly at batch {bi + 1}; rerun with --resume")
                 return
             if a.stop_after and n_done >= a.stop_after:
                 log(f"[atlas] stopping after {n_done} batches (simulated cap)")
+                writer.wait()
                 if rank == 0:
                     (out / "run.json").write_text(json.dumps(summary(False, bi + 1), indent=1))
                 return
+    writer.wait()
     logf.close()
     atlas.check_errors()
     if world > 1:

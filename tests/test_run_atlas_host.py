@@ -63,3 +63,26 @@ def test_range_attribution_of_a_trace(tmp_path):
     assert res["_total"]["busy_us"] == 53.0 and res["_total"]["count"] == 4
     txt = table(res)
     assert "atlas.merge.top" in txt and "filter_bulk_kernel" in txt
+
+
+def test_checkpoint_writer_background_keeps_last_two_and_runs_follow_up(tmp_path):
+    from proteus_b200.run_atlas import CheckpointWriter
+    w = CheckpointWriter(tmp_path, keep=2)
+    done = []
+    for nb in (5, 10, 15):
+        w.save(_ckpt(nb), tmp_path / f"ckpt_{nb}.pt", after=lambda nb=nb: done.append(nb))
+    w.wait()
+    assert sorted(p.name for p in tmp_path.iterdir()) == ["ckpt_10.pt", "ckpt_15.pt"]
+    assert done == [5, 10, 15]  # one write at a time, in order, each follow-up after its file
+    p, st = load_latest_ckpt(tmp_path)
+    assert p.name == "ckpt_15.pt" and torch.equal(st["atlas"]["top_s"], torch.arange(6.0))
+
+
+def test_checkpoint_writer_reports_a_failed_write(tmp_path):
+    import pytest
+    from proteus_b200.run_atlas import CheckpointWriter
+    w = CheckpointWriter(tmp_path / "missing_dir")
+    w.save(_ckpt(5), tmp_path / "missing_dir" / "ckpt_5.pt")
+    with pytest.raises((FileNotFoundError, RuntimeError), match="does not exist|No such file"):
+        w.wait()
+    w.wait()  # the error is reported once
