@@ -648,16 +648,20 @@ def main():
         bytes_launch = (valid_rows * D * 2 + rows * 4) / K + comp * 12 / (K * L) + 2 * D * 4
         achieved = bytes_launch / filt_ms / 1e6
         value = tok_all / (ms_max / 1e3)
-        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        c4 = args.model == "650M"
+        wl = (f"{'C4' if c4 else 'C4 stream on ' + args.model}: ESM-2 {args.model} forward + streaming atlas "
+              f"({L} layers x {D} units x 2 poles)")
+        line = {"metric": METRIC if c4 else METRIC.replace("650M", args.model), "value": value, "unit": "tokens/s",
+                "n_gpus": world, "steps": K, "warmup": W,
                 "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "C4: ESM-2 650M forward + streaming atlas (33 layers x 5120 units x 2 poles)",
-                           "model": "ESM-2 650M architecture, random init seed 0, bf16", "K": args.K, "Kr": args.Kr,
+                "config": {"workload": wl,
+                           "model": f"ESM-2 {args.model} architecture, random init seed 0, bf16", "K": args.K, "Kr": args.Kr,
                            "bins": 5, "tokens_per_batch": args.tokens_per_batch, "pilot_seqs": args.pilot_seqs,
                            "stream_sequences": args.n_seqs, "stream_tokens": n_total,
                            "pilot_tokens": n_pilot, "seeded": True, "parallelism": f"dp{world} (sequence shards)",
                            "timed_from_batch": P + W, "stream_tokens_before_timed": atlas_tokens_before,
-                           "l2": "inputs larger than L2: each layer's activation block is ~335 MB",
+                           "l2": f"inputs larger than L2: each layer's activation block is ~{rows / K * D * 2 / 1e6:.0f} MB",
                            "valid_tokens_per_step": valid_rows / K, "padded_rows_per_step": rows / K},
                 "atlas_overhead_vs_forward": ms_max / fwd_max - 1.0, "forward_only_ms_per_step": fwd_max / K,
                 "e2e": {"value": e2e_tok / (e2e_max / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d / K,

@@ -44,11 +44,12 @@ def test_filter_matches_reference(case, dtype):
     assert int(cnt64) == n  # overflow: exact count, nothing past cap
 
 
-def test_filter_large_vector_path():
-    """bf16 16-byte vector path at a B200-sized shape with a padding mix and -inf thresholds."""
+@pytest.mark.parametrize("T,D", [(4099, 5120), (1031, 10240)])
+def test_filter_large_vector_path(T, D):
+    """bf16 16-byte vector path at B200-sized shapes (ESM-2 650M and 3B FFN widths) with a padding
+    mix and -inf thresholds."""
     KN = _kn()
     g = torch.Generator(device=DEV).manual_seed(0)
-    T, D = 4099, 5120
     H = (torch.randn(T, D, generator=g, device=DEV) * 2).to(torch.bfloat16)
     valid = torch.rand(T, generator=g, device=DEV) > 0.1
     rowmap = torch.full((T,), -1, dtype=torch.int64, device=DEV)
@@ -198,7 +199,7 @@ def test_sub_stats_bf16_edge_ties():
         assert torch.equal(M[1, j].cpu(), m1), j
 
 
-@pytest.mark.parametrize("n,D", [(1600, 5120), (301, 1000), (77, 96), (4096, 640), (700, 3900)])
+@pytest.mark.parametrize("n,D", [(1600, 5120), (301, 1000), (77, 96), (4096, 640), (700, 3900), (300, 10240)])
 def test_gram_upper_blocks(n, D):
     """gram_accumulate semantics: two accumulations, rel-max error < 1e-5 vs fp64 (reference
     test tolerance, tests/test_stats_triton.py:74), lower 128-blocks untouched."""
