@@ -1,16 +1,19 @@
 // K1: single-pass compare-and-compact over the hook output H (one read of H per layer).
 //
-// Replaces filter_candidates (atlas/filter_triton.py:19-86). B200 layout: each warp owns a strip of
-// 32 * VEC consecutive columns (one 16-byte vector per lane, VEC = 8 for bf16/fp16, 4 for fp32) and
-// walks rows with U rows in flight per lane; the per-column thresholds live in registers for the
-// whole walk. Padding rows (rowmap < 0) are never read.
-// Compaction is two-level: a warp ballot + shuffle prefix sum places a step's survivors in a
-// per-CTA staging area in shared memory (one shared-memory atomic per warp step with hits), and
-// the CTA reserves its global output range with ONE global atomic at the end, then copies the
-// staged survivors out with coalesced stores. At ~0.1-0.5% survivors nearly every warp step has a
-// hit, so per-step global atomics on the single counter would serialise the whole pass; a warp
-// whose step does not fit the staging area writes directly (global atomic), which keeps the
-// count exact for any survivor density.
+// Replaces filter_candidates (atlas/filter_triton.py:19-86). Two kernels, one contract:
+//  * bf16 with 16-byte-aligned rows (the hot case): filter_bulk_kernel, TMA-fed (see its section
+//    below): a producer warp streams 32-row x 256-column tiles through shared memory, consumer warps
+//    compare packed bf16 pairs and park rare hits in per-warp queues.
+//  * fp16 / fp32 and unaligned shapes: filter_kernel, register-fed: each warp owns a strip of
+//    32 * VEC consecutive columns (one 16-byte vector per lane, VEC = 8 for 16-bit types, 4 for
+//    fp32, 1 when unaligned) and walks rows with U rows in flight per lane; the per-column
+//    thresholds live in registers for the whole walk.
+// Padding rows (rowmap < 0) are never read by the register path and never copied by the TMA path
+// unless they share a 32-row tile with a valid row. Compaction is two-level in both: survivors are
+// staged per CTA in shared memory, and the CTA reserves its global output range with ONE global
+// atomic at the end and copies them out with coalesced stores (per-step global atomics on the one
+// counter would serialise the pass at ~0.1-0.5% survivors); survivors that do not fit the staging
+// area go straight to the global list, so the count stays exact for any survivor density.
 #include "tc.cuh"
 
 namespace atlas {
@@ -21,20 +24,6 @@ namespace {
 template <int DT, int VEC>
 struct Vec;
 
-#ifndef ATLAS_FILTER_PACKED
-#define ATLAS_FILTER_PACKED 1  // bf16 vector path: packed compares + software pipeline (filter_bf16_kernel)
-#endif
-#if !ATLAS_FILTER_PACKED
-template <>
-struct Vec<ATLAS_BF16, 8> {
-  uint4 v;
-  __device__ __forceinline__ void load(const void* p) { v = __ldcs(reinterpret_cast<const uint4*>(p)); }
-  __device__ __forceinline__ float at(int k) const {
-    const uint32_t w = k < 2 ? v.x : k < 4 ? v.y : k < 6 ? v.z : v.w;
-    return (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
-  }
-};
-#endif
 template <>
 struct Vec<ATLAS_F16, 8> {
   uint4 v;
@@ -182,23 +171,12 @@ filter_kernel(const char* __restrict__ H, int64_t T, int64_t D, int64_t ld_bytes
   }
 }
 
-// bf16 fast path. Same contract as filter_kernel, built to spend few instructions per byte:
-//  * compares run on packed bf16 pairs against thresholds rounded to bf16 (toward -inf for the
-//    positive pole, toward +inf for the negative pole). For a bf16 value h and an fp32 threshold t,
-//    h > t  <=>  h > rd_bf16(t)  and  h < t  <=>  h < ru_bf16(t) (no bf16 lies strictly between
-//    t and its directed rounding), so the survivors are exactly those of the fp32 comparison;
-//    NaN compares false on both sides as in fp32. Each 32-bit word gives a hit mask (0xFFFF per
-//    surviving half) that is kept for the extraction below;
-//  * survivors are rare (a lane sees one in ~5% of its steps), so a lane with hits takes its
-//    slots one by one with a shared-memory atomic: no warp vote or scan on the common path;
-//  * optional overlap (ATLAS_FILTER_PIPE): flagged rows are parked in shared memory so the next
-//    step's loads go out before the survivors are extracted;
-//  * the row map is read once per 32 rows of a warp (one lane per row, one block ahead) and
-//    handed out with shuffles, so no H load waits on a dependent row-map load.
-#ifndef ATLAS_FILTER_PIPE
-#define ATLAS_FILTER_PIPE 0
-#endif
-
+// ------------------------------------------------------------------ bf16 compare and emit helpers
+// Compares run on packed bf16 pairs against thresholds rounded to bf16 (toward -inf for the
+// positive pole, toward +inf for the negative pole). For a bf16 value h and an fp32 threshold t,
+// h > t  <=>  h > rd_bf16(t)  and  h < t  <=>  h < ru_bf16(t) (no bf16 lies strictly between t and
+// its directed rounding), so the survivors are exactly those of the fp32 comparison; NaN compares
+// false on both sides as in fp32.
 template <int N>
 struct StageAreaN {
   static constexpr int kCap = N;
@@ -264,22 +242,6 @@ __device__ __forceinline__ uint32_t bf16_flags(const uint4 (&x)[U], const int32_
   return flags;
 }
 
-// Survivors of one flagged row vector: rebuild its 8-bit mask and emit them one by one.
-template <class SA>
-__device__ __forceinline__ void bf16_emit_row(const uint4& x, int32_t row, const __nv_bfloat162 (&tp2)[4],
-                                              const __nv_bfloat162 (&tn2)[4], int c0, SA& sa,
-                                              float* __restrict__ out_val, int32_t* __restrict__ out_row,
-                                              int32_t* __restrict__ out_col, int32_t* __restrict__ count, int64_t cap) {
-  uint32_t b = hit_bits8(x, tp2, tn2);
-  while (b) {
-    const int k = __ffs(b) - 1;
-    b &= b - 1;
-    const uint32_t w = k < 2 ? x.x : k < 4 ? x.y : k < 6 ? x.z : x.w;
-    const float h = (k & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
-    emit_one(sa, h, row, c0 + k, out_val, out_row, out_col, count, cap);
-  }
-}
-
 // Survivors of one step of a lane (rows flagged in `flags`): the 8-bit masks of the flagged rows,
 // ONE shared-memory reservation for all of them, then plain stores. Slots past the staging area go
 // straight to the global list (global atomic per survivor; the count stays exact past `cap`).
@@ -322,128 +284,7 @@ __device__ __forceinline__ void bf16_emit_step(uint32_t flags, const uint4 (&x)[
   }
 }
 
-template <int U>
-__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
-filter_bf16_kernel(const char* __restrict__ H, int T, int D, int64_t ld_bytes, int rows_per_cta,
-                   const int32_t* __restrict__ rowmap, const float* __restrict__ thr_pos,
-                   const float* __restrict__ thr_neg, float* __restrict__ out_val, int32_t* __restrict__ out_row,
-                   int32_t* __restrict__ out_col, int32_t* __restrict__ count, int64_t cap) {
-  static_assert(32 % U == 0, "U must divide 32");
-  constexpr int kIpb = 32 / U;  // steps per row-map block
-  const int lane = threadIdx.x & 31;
-  const int warp = (threadIdx.x >> 5) / kWX;
-  const int wx = (threadIdx.x >> 5) % kWX;
-  const int c0 = ((blockIdx.x * kWX + wx) * 32 + lane) * 8;  // D < 2^31 (host check)
-  const bool col_ok = c0 < D;  // 8 divides D on this path, so a lane's 8 columns are all in or all out
-  __nv_bfloat162 tp2[4], tn2[4];
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    __nv_bfloat16 p[2], n[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = c0 + 2 * w + h;
-      p[h] = __float2bfloat16_rd(col_ok ? __ldg(thr_pos + c) : __int_as_float(0x7F800000));
-      n[h] = __float2bfloat16_ru(col_ok ? -__ldg(thr_neg + c) : __int_as_float(0xFF800000));
-    }
-    tp2[w] = __halves2bfloat162(p[0], p[1]);
-    tn2[w] = __halves2bfloat162(n[0], n[1]);
-  }
-  __shared__ StageArea sa;
-  __shared__ int s_base;
-  if (threadIdx.x == 0) sa.n = 0;
-  __syncthreads();
-  const int r_begin = blockIdx.y * rows_per_cta;
-  const int r_end = min(r_begin + rows_per_cta, T);
-  const int rbase = r_begin + warp;  // this warp's rows: rbase + j * kWY, j = 0, 1, ...
-  const int n_rows = r_end > rbase ? (r_end - rbase + kWY - 1) / kWY : 0;
-  const int n_steps = (n_rows + U - 1) / U;
-  auto rm_block = [&](int b) -> int32_t {  // row-map entries of rows b*32 .. b*32+31 of this warp
-    const int row = rbase + (b * 32 + lane) * kWY;
-    return (row < r_end && col_ok) ? __ldg(rowmap + row) : -1;
-  };
-  int32_t rm_cur = rm_block(0), rm_nxt = rm_block(1);
-  const int64_t rstride = (int64_t)kWY * ld_bytes;  // bytes between a warp's consecutive rows
-  const char* p = H + (int64_t)rbase * ld_bytes + c0 * 2;  // row of the step being loaded
-#if ATLAS_FILTER_PIPE
-  // A lane with hits parks the flagged rows of its step in shared memory, issues the next step's
-  // loads, and extracts the survivors while those loads are in flight.
-  __shared__ uint4 s_x[kWarps * 32][U];
-  __shared__ int32_t s_v[kWarps * 32][U];
-  uint4 x[U];
-  int32_t v[U];
-#pragma unroll
-  for (int u = 0; u < U; ++u) {
-    v[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, u);
-    if (v[u] >= 0) x[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
-  }
-  for (int it = 0; it < n_steps; ++it) {
-    const uint32_t flags = bf16_flags<U>(x, v, tp2, tn2);
-    if (flags) {
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (flags & (1u << u)) {
-          s_x[threadIdx.x][u] = x[u];
-          s_v[threadIdx.x][u] = v[u];
-        }
-    }
-    const int jt = it + 1;  // the step loaded now
-    if (jt % kIpb == 0) {
-      rm_cur = rm_nxt;
-      rm_nxt = rm_block(jt / kIpb + 1);
-    }
-    const int sub = (jt % kIpb) * U;
-    p += U * rstride;
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      v[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, sub + u);
-      if (v[u] >= 0) x[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
-    }
-    if (flags) {
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (flags & (1u << u))
-          bf16_emit_row(s_x[threadIdx.x][u], s_v[threadIdx.x][u], tp2, tn2, c0, sa, out_val, out_row, out_col, count, cap);
-    }
-  }
-#else
-  for (int it = 0; it < n_steps; ++it) {
-    if (it > 0 && it % kIpb == 0) {
-      rm_cur = rm_nxt;
-      rm_nxt = rm_block(it / kIpb + 1);
-    }
-    const int sub = (it % kIpb) * U;
-    uint4 x[U];
-    int32_t v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      v[u] = __shfl_sync(0xFFFFFFFFu, rm_cur, sub + u);
-      if (v[u] >= 0) x[u] = __ldcs(reinterpret_cast<const uint4*>(p + u * rstride));
-    }
-    p += U * rstride;
-    const uint32_t flags = bf16_flags<U>(x, v, tp2, tn2);
-    if (flags) {
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (flags & (1u << u)) bf16_emit_row(x[u], v[u], tp2, tn2, c0, sa, out_val, out_row, out_col, count, cap);
-    }
-  }
-#endif
-  __syncthreads();
-  const int staged_n = sa.n < kStage ? sa.n : kStage;  // slots [0, staged_n) are all staged
-  if (threadIdx.x == 0) s_base = staged_n > 0 ? atomicAdd(count, staged_n) : 0;
-  __syncthreads();
-  const int64_t base = s_base;
-  for (int i = threadIdx.x; i < staged_n; i += blockDim.x) {
-    const int64_t slot = base + i;
-    if (slot < cap) {
-      out_val[slot] = sa.val[i];
-      out_row[slot] = sa.row[i];
-      out_col[slot] = sa.col[i];
-    }
-  }
-}
-
-// ------------------------------------------------------------------ bf16, bulk-copy fed (default)
+// ------------------------------------------------------------------ bf16, TMA-fed
 // The strip of 256 columns (512 bytes per row) a CTA owns is streamed through a ring of shared
 // memory stages by TMA: one 2-D tile copy of 32 rows x 256 columns (16 KB) per stage, completion
 // counted on an mbarrier. The bytes in flight are bounded by shared memory (kBStages x 16 KB per
@@ -452,13 +293,11 @@ filter_bf16_kernel(const char* __restrict__ H, int T, int D, int64_t ld_bytes, i
 // bulk copies saturated it at about half the HBM bandwidth). Warp kBWarps produces (row-map
 // entries four stages ahead; a stage of padding rows only is not copied), warps 0..kBWarps-1
 // consume 4 rows of each stage (one 16-byte vector per lane per row, read from shared memory),
-// release the stage as soon as their vectors are in registers, then compare and emit as
-// filter_bf16_kernel does. Padding rows inside a stage are copied with it and skipped. Every wait is bounded; a wait that gives up records a code in the
-// device status word and the CTA finishes (the producer first waits, again bounded, for the
-// copies it issued).
-#ifndef ATLAS_FILTER_BULK
-#define ATLAS_FILTER_BULK 1
-#endif
+// release the stage as soon as their vectors are in registers, then compare (per-row "any hit"
+// flags) and park flagged row vectors in the warp's hit queue. Padding rows inside a stage are
+// copied with it and skipped. Every wait is bounded; a wait that gives up records a code in the
+// device status word and the CTA finishes (the producer first waits, again bounded, for the copies
+// it issued).
 #ifndef ATLAS_FILTER_BSTAGES
 #define ATLAS_FILTER_BSTAGES 3
 #endif
@@ -724,12 +563,8 @@ int launch(const void* H, int64_t T, int64_t D, int64_t ld, const int32_t* rowma
                 (long long)T, (long long)D);
   dim3 grid((unsigned)strips, (unsigned)chunks);
   const int64_t ld_bytes = ld * (int64_t)sizeof(typename Elem<DT>::T);
-  if constexpr (DT == ATLAS_BF16 && VEC == 8 && ATLAS_FILTER_PACKED)
-    filter_bf16_kernel<U><<<grid, kWarps * 32, 0, st>>>(reinterpret_cast<const char*>(H), (int)T, (int)D, ld_bytes,
-                                                        (int)rows, rowmap, tp, tn, ov, orow, ocol, count, cap);
-  else
-    filter_kernel<DT, VEC, U><<<grid, kWarps * 32, 0, st>>>(reinterpret_cast<const char*>(H), T, D, ld_bytes, rows,
-                                                            rowmap, tp, tn, ov, orow, ocol, count, cap);
+  filter_kernel<DT, VEC, U><<<grid, kWarps * 32, 0, st>>>(reinterpret_cast<const char*>(H), T, D, ld_bytes, rows,
+                                                          rowmap, tp, tn, ov, orow, ocol, count, cap);
   return check_launch("atlas_filter_compact");
 }
 
@@ -763,11 +598,8 @@ extern "C" int atlas_filter_compact(const void* H, int dtype, int64_t T, int64_t
   const uintptr_t a = (uintptr_t)H;
   switch (dtype) {
     case ATLAS_BF16:
-      if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0) {
-        if (ATLAS_FILTER_BULK)
-          return launch_bulk(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
-        return launch<ATLAS_BF16, 8, ATLAS_FILTER_U>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
-      }
+      if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0)
+        return launch_bulk(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
       return launch<ATLAS_BF16, 1, 4>(H, T, D, ld, rowmap, thr_pos, thr_neg, out_val, out_row, out_col, count, cap, st);
     case ATLAS_F16:
       if (D % 8 == 0 && ld % 8 == 0 && a % 16 == 0)

@@ -19,7 +19,7 @@ def _kn():
 
 
 @pytest.mark.parametrize("case", range(len(FILTER_CASES)))
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_filter_matches_reference(case, dtype):
     """Survivor set, values and count of filter_candidates (filter_triton.py:65-86) — bit-exact,
     including the exact count when the output buffer overflows (cap 64)."""
