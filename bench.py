@@ -375,7 +375,74 @@ def kernel_microbench(dev, peaks, reps=20):
     bytes_ = n_c * 24 + G * K * 20 * 2
     out["merge_c2"] = {"G": G, "K": K, "candidates": n_c, "ms_per_call": ms, "bytes": bytes_,
                        "GBps": bytes_ / ms / 1e6, "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"]}
+    del st_sc, st_tok, st_val, sets
+    out["c2_stream"] = c2_stream(dev, peaks, scale, shift)
     return out
+
+
+@torch.no_grad()
+def c2_stream(dev, peaks, scale, shift, n_blocks=64, warm=8, T=16384, D=5120):
+    """C2 as a stream: the drop-in Atlas (1 layer, both poles, K=100, Kr=32, 5 bins; no subsample
+    statistics, which belong to C3) over the first `n_blocks` of C2's 200 heavy-tailed [16384 x 5120]
+    bf16 blocks,
+    pre-generated in HBM. Edges at the (0.5, 0.9, 0.99, 0.999, 0.9999) column quantiles and seeds
+    (top-K tau, reservoir key ceilings sized for c*Kr) from a pilot block; token ids seq*1024+pos over
+    64 sequences x 256 positions, re-labelled per block. Each block is begin_batch + observe (filter,
+    bulk rows, predicated dense path) + end_batch (admission and both merges): blocks/s and the H
+    bytes streamed per second."""
+    from proteus_b200.core import Atlas, AtlasConfig
+    from proteus_b200.pilot import pilot_edges, pilot_seeds
+    g = torch.Generator(device=dev).manual_seed(23)
+
+    def block():
+        t = torch.distributions.StudentT(torch.tensor(3.0, device=dev)).sample((T, D))
+        return (t * scale + shift).to(torch.bfloat16)
+
+    pilot_H = block()[:2048].float()
+    E = pilot_edges([pilot_H])
+    n_total = 200 * T  # C2's stream length: the reservoir key ceilings are sized for 200 blocks
+    _, rk = pilot_seeds([pilot_H], E, 100, 32, n_total)
+    # top-K tau at the 99.9% column quantile of each pole (the C2 threshold), as a strict lower bound
+    q = torch.stack([torch.quantile(pilot_H, 0.999, dim=0), torch.quantile(-pilot_H, 0.999, dim=0)])
+    ts = torch.nextafter(q, torch.full_like(q, float("-inf"))).view(1, 2, D)
+    del pilot_H
+    cfg = AtlasConfig(K=100, Kr=32, seed=0, subsample=False, gram=False)
+    at = Atlas(1, D, E, cfg, device=dev)
+    at.seed(ts, rk)
+    seq_pos = torch.arange(T)
+    blocks, ctxs = [], []
+    for b in range(n_blocks):
+        blocks.append(block())
+        tok = ((seq_pos // 256) + 64 * b) * 1024 + seq_pos % 256
+        ctxs.append(at.make_ctx(T, torch.arange(T), tok))  # built on the atlas's device
+    torch.cuda.synchronize()
+
+    def run(i):
+        at.begin_batch(ctxs[i])
+        at.observe(0, blocks[i])
+        at.end_batch()
+
+    for i in range(warm):
+        run(i)
+    torch.cuda.synchronize()
+    st0 = at.stats
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(warm, n_blocks):
+        run(i)
+    b.record()
+    torch.cuda.synchronize()
+    at.check_errors()
+    ms = a.elapsed_time(b) / (n_blocks - warm)
+    st1 = at.stats
+    h_bytes = T * D * 2
+    res = {"blocks_timed": n_blocks - warm, "ms_per_block": ms, "blocks_per_s": 1e3 / ms,
+           "H_GBps": h_bytes / ms / 1e6, "frac_hbm_H": h_bytes / ms / 1e6 / peaks["hbm_gbs"],
+           "per_block": {k: (st1[k] - st0.get(k, 0)) / (n_blocks - warm) for k in ("compacted", "top_cand", "res_cand")},
+           "dense_layer_batches": st1["dense_layer_batches"] - st0.get("dense_layer_batches", 0)}
+    del blocks, ctxs, at
+    torch.cuda.empty_cache()
+    return res
 
 
 # ----------------------------------------------------------------------------- CPU side (oracle)
