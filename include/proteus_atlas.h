@@ -116,6 +116,19 @@ int atlas_count_gemm_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int
 int atlas_gram_upper(const void* XT, int dtype, int64_t ldx, int64_t n, int64_t D, float* C, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Per-batch counters of end_batch — the bookkeeping of _merge_filtered_impl's counts read
+ * (atlas/core.py:458-470), kept on the device instead of read on the host: one thread adds
+ *   stats[0] += sum of count[l] over filtered layers (filtered_host[l] != 0) with count[l] <= cap(l)
+ *   stats[1] += *n_top,  stats[2] += *n_res  (records admitted this batch)
+ *   stats[3] += number of filtered layers with count[l] > cap(l) (each took the dense path)
+ * cap(l) = l < early_layers ? cap_early : cap_main. filtered_host is a HOST array of L bytes (may be
+ * NULL: no filtered layer); L <= 64. stats: int64[4] on the device.
+ */
+int atlas_batch_counters(const int32_t* count, int64_t L, const int8_t* filtered_host, int64_t cap_main,
+                         int64_t cap_early, int64_t early_layers, const int32_t* n_top, const int32_t* n_res,
+                         int64_t* stats, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Candidate admission for the filtered layers of a batch — replaces _merge_filtered_impl's
  * candidate tests and the bulk-row paths _bulk_loop / _bulk_stacked (atlas/core.py:482-590).
  * For every layer l with layer_mode[l] == 1 and count[l] <= cap(l):

@@ -547,21 +547,14 @@ class Atlas:
                                          rcap, self._ws_res)
 
     def _count_batch(self, L, c, filt, fl, cap_main, cap_early):
+        """Survivors of the non-overflowed filtered layers, records admitted, overflowed layers (each
+        took the dense path): added to the device counters by one kernel, no host read."""
+        fmask = torch.zeros(L, dtype=torch.int8)
         if filt:
-            caps = torch.tensor([cap_early if (c.cap_frac_early > 0 and l < c.early_layers) else cap_main
-                                 for l in range(L)], dtype=torch.int32).to(self.dev, non_blocking=True)
-            fmask = torch.zeros(L, dtype=torch.bool)
-            fmask[filt] = True
-            fmask = fmask.to(self.dev, non_blocking=True)
-            cnt = self._counts.to(torch.int64)
-            ok = fmask & (self._counts <= caps)
-            over = fmask & (self._counts > caps)
-            upd = torch.stack([(cnt * ok).sum(), fl[L].to(torch.int64), fl[L + 1].to(torch.int64),
-                               over.sum().to(torch.int64)])
-        else:
-            upd = torch.stack([torch.zeros((), dtype=torch.int64, device=self.dev), fl[L].to(torch.int64),
-                               fl[L + 1].to(torch.int64), torch.zeros((), dtype=torch.int64, device=self.dev)])
-        self._dev_stats += upd
+            fmask[filt] = 1
+        early = c.early_layers if c.cap_frac_early > 0 else 0
+        call("atlas_batch_counters", ptr(self._counts), L, fmask.data_ptr(), cap_main, cap_early, early,
+             ptr(fl[L:L + 1]), ptr(fl[L + 1:L + 2]), ptr(self._dev_stats), stream_ptr(self.dev))
 
     def check_errors(self):
         """Raise if a device-side list ran out of capacity (never expected: lists are sized for the

@@ -365,6 +365,44 @@ int esize(int dtype) { return dtype == ATLAS_F32 ? 4 : 2; }
 
 using namespace atlas;
 
+namespace atlas {
+namespace {
+__global__ void batch_counters_kernel(const int32_t* __restrict__ count, int L, uint64_t filt, int64_t cap_main,
+                                      int64_t cap_early, int early_layers, const int32_t* __restrict__ n_top,
+                                      const int32_t* __restrict__ n_res, int64_t* __restrict__ stats) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  int64_t compacted = 0, over = 0;
+  for (int l = 0; l < L; ++l) {
+    if (!((filt >> l) & 1ull)) continue;
+    const int64_t cap = l < early_layers ? cap_early : cap_main;
+    const int64_t c = count[l];
+    if (c <= cap)
+      compacted += c;
+    else
+      ++over;
+  }
+  stats[0] += compacted;
+  stats[1] += *n_top;
+  stats[2] += *n_res;
+  stats[3] += over;
+}
+}  // namespace
+}  // namespace atlas
+
+extern "C" int atlas_batch_counters(const int32_t* count, int64_t L, const int8_t* filtered_host, int64_t cap_main,
+                                    int64_t cap_early, int64_t early_layers, const int32_t* n_top, const int32_t* n_res,
+                                    int64_t* stats, void* stream) {
+  ATLAS_REQUIRE(L >= 0 && L <= 64, "batch_counters: L must be 0..64 (got %lld)", (long long)L);
+  ATLAS_REQUIRE(count && n_top && n_res && stats, "batch_counters: null pointer");
+  uint64_t filt = 0;
+  if (filtered_host)
+    for (int64_t l = 0; l < L; ++l)
+      if (filtered_host[l]) filt |= 1ull << l;
+  batch_counters_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(count, (int)L, filt, cap_main, cap_early, (int)early_layers,
+                                                           n_top, n_res, stats);
+  return check_launch("atlas_batch_counters");
+}
+
 extern "C" int atlas_thresholds(const float* top_s, int64_t K, const int64_t* res_s, int64_t Kr, const float* top_seed,
                                 const int64_t* res_seed, const float* E, int64_t G, int64_t B, int64_t U_res,
                                 int reservoir, float* thr, void* stream) {

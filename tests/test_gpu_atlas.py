@@ -57,6 +57,10 @@ def test_stream_matches_reference(name):
     got = at.result()
     bad = compare(got, z, fields=EXACT_FIELDS)
     assert not bad, bad
+    # the Atlas.stats counters of the reference (core.py:198-199); top_cand / res_cand are left out:
+    # in dense bursts the reference counts every element tied at the K-th value, this build the top-K
+    for k in ("batches", "elements", "compacted", "redo_layers", "dense_layer_batches"):
+        assert got["stats"][k] == int(z["stat_" + k]), (k, got["stats"][k], int(z["stat_" + k]))
     # moments and Gram against the oracle's fp64 sums / the reference's Gram
     oc = O.OracleConfig(**STREAM_CFG, **ckw)
     oa = O.AtlasOracle(st.L, st.D, z["E"], oc, n_annot=STREAM_SHAPE["n_annot"])
