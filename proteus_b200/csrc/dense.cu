@@ -116,18 +116,15 @@ struct ColShared {
   Staged st;
 };
 
+// One column d of the layer (the CTA's threads together): top-K radix select and reservoir runs.
 template <int DT>
-__global__ void __launch_bounds__(kThreads)
-dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
-                    const int64_t* __restrict__ key, const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
-                    int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
-                    const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
-                    const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
-                    int64_t cap, int force, Lists top, Lists res, int32_t* __restrict__ err) {
-  if (!triggered(count, cap, force)) return;
-  extern __shared__ __align__(16) unsigned char col_raw[];
-  ColShared& sh = *reinterpret_cast<ColShared*>(col_raw);
-  const int64_t d = blockIdx.x;
+__device__ __forceinline__ void dense_column(ColShared& sh, int64_t d, const typename Elem<DT>::T* __restrict__ HT,
+                                             int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
+                                             const int64_t* __restrict__ key, const int32_t* __restrict__ key_order,
+                                             int64_t layer, int64_t D, int B, int64_t K, int64_t Kr, int reservoir,
+                                             const float* __restrict__ top_seed, const int64_t* __restrict__ top_k,
+                                             const int64_t* __restrict__ res_s, const int64_t* __restrict__ res_seed,
+                                             const float* __restrict__ E, Lists top, Lists res, int32_t* __restrict__ err) {
   const typename Elem<DT>::T* col = HT + d * ldh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool select_all = n_v <= K;
@@ -346,6 +343,26 @@ dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, in
   flush(sh.st, res, err, &sh.base);
 }
 
+// Columns are taken grid-stride by at most one resident wave of CTAs, so an untriggered launch costs
+// about a wave of early exits rather than one CTA per column.
+template <int DT>
+__global__ void __launch_bounds__(kThreads)
+dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
+                    const int64_t* __restrict__ key, const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
+                    int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
+                    const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
+                    const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
+                    int64_t cap, int force, Lists top, Lists res, int32_t* __restrict__ err) {
+  if (!triggered(count, cap, force)) return;
+  extern __shared__ __align__(16) unsigned char col_raw[];
+  ColShared& sh = *reinterpret_cast<ColShared*>(col_raw);
+  for (int64_t d = blockIdx.x; d < D; d += gridDim.x) {
+    dense_column<DT>(sh, d, HT, ldh, n_v, tok, key, key_order, layer, D, B, K, Kr, reservoir, top_seed, top_k, res_s,
+                     res_seed, E, top, res, err);
+    __syncthreads();  // the next column re-initialises the shared state
+  }
+}
+
 template <int DT>
 int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int32_t* valid_rows, int64_t n_v,
                  const int64_t* tok, const int64_t* key, const int32_t* key_order, int64_t B, int64_t K, int64_t Kr,
@@ -363,7 +380,13 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   const size_t smem = sizeof(ColShared);
   if (cudaFuncSetAttribute(dense_column_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return fail(ATLAS_ERR_CUDA, "dense_select: cannot reserve %zu bytes of shared memory", smem);
-  dense_column_kernel<DT><<<(unsigned)D, kThreads, smem, st>>>(HT, n8, n_v, tok, key, key_order, layer, D, (int)B, K, Kr,
+  static int per_sm = 0;  // resident CTAs per SM (registers bound it), queried once per instantiation
+  if (per_sm == 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_column_kernel<DT>, kThreads, smem) !=
+                          cudaSuccess ||
+                      per_sm < 1))
+    per_sm = 1;
+  const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
+  dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, key, key_order, layer, D, (int)B, K, Kr,
                                                                 reservoir, top_seed, top_k, res_s, res_seed, E, count,
                                                                 cap, force, top, res, err);
   return check_launch("atlas_dense_select: column");

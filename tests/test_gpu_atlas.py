@@ -112,6 +112,24 @@ def test_checkpoint_roundtrip_and_resume():
     assert ga["n_seen"] == gb["n_seen"]
 
 
+def test_dense_path_wide_layer_matches_oracle():
+    """The dense path over more columns than one resident wave of CTAs (D = 1280: each CTA takes
+    several columns in turn). Unseeded, so the first batch is dense in every column; later batches
+    filter, and the cap sends some layer-batches back to the dense path (4 dense, 3 filtered). Every
+    exact field against the oracle on the same activations."""
+    st = make_stream(L=1, D=1280, n_seq=90, seed=21, dtype="bf16", n_annot=5, bmin=6, bmax=20)
+    E = O.pilot_edges([st.batches[0].H[0][st.batches[0].valid_rows]])
+    cfg = dict(K=8, Kr=4, rho_res=0.05, rho_sub=0.2, cap_frac=0.05, seed=13, stats_impl="v1", merge_impl="loop")
+    at = run_cuda(st, E, cfg, None, n_annot=5)
+    got = at.result()
+    oa = O.AtlasOracle(st.L, st.D, E, O.OracleConfig(**cfg), n_annot=5)
+    drive(oa, st)
+    want = oa.result()
+    bad = compare(got, want, fields=EXACT_FIELDS)
+    assert not bad, bad
+    assert got["stats"]["dense_layer_batches"] == want["stats"]["dense_layer_batches"] >= 1
+
+
 def test_merge_from_matches_reference():
     """Two CUDA shards over interleaved halves, seeded from the global stream, merged with the GPU
     merge_from == the reference's merged result (tests/test_resume_merge.py:47-98)."""
