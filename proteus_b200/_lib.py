@@ -85,6 +85,8 @@ LAUNCHES = {"count": 0}
 def _n_kernels(name: str, args) -> int:
     if name == "atlas_dense_select":
         return 3 if args[14] else 1
+    if name == "atlas_admit":  # candidates, plus the bulk-row kernel when there are bulk rows
+        return 2 if (args[6] and args[20]) else 1
     if name.endswith("_bytes") or name.endswith("_i32"):
         return 0
     return _KERNELS.get(name, 1)

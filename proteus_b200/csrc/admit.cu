@@ -100,38 +100,80 @@ admit_kernel(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t U_r
       warp_append(lane, nt, tg, tsc, tt, tv, o.tg, o.tsc, o.ttok, o.tval, o.nt, o.tcap, o.err);
       warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
     }
-    // ---- bulk rows (key < U_res): every element is a reservoir candidate
-    if (!reservoir || n_r == 0) continue;
-    const int64_t nb = n_r * D;
-    for (int64_t base = warp_id * 32; base < nb; base += n_warps * 32) {
-      const int64_t e = base + lane;
-      int nr = 0;
-      int32_t rg[2];
-      int64_t rsc[2], rt[2];
-      float rv[2];
-      if (e < nb) {
-        const int64_t i = e / D, col = e - i * D;
-        const float h = ld_elem<RT>(R + (l * r_stride + i) * D + col);
-        const int32_t vi = bulk_vidx[i];
-        const int64_t tk = tok[vi], ky = key[vi];
+  }
+}
+
+// Bulk rows (key < U_res; every element is a reservoir candidate), one thread per (layer, column,
+// chunk of kAdmRows rows): the column's bin edges and reservoir thresholds (max of the Kr-th state
+// key and the seed) of both poles are loaded once into registers, then the thread walks its rows
+// (R read coalesced along the columns, the row's key broadcast). Loading the thresholds per element instead
+// made every element fetch a scattered 8-byte slot per pole.
+constexpr int kAdmB = 8;
+constexpr int kAdmRows = 16;  // bulk rows per CTA (grid z): enough CTAs even for one layer
+
+template <typename RT>
+__global__ void __launch_bounds__(256)
+admit_bulk_kernel(int64_t L, int64_t D, int B, int64_t Kr, uint64_t mode_mask, const int32_t* __restrict__ count,
+                  int64_t cap_main, int64_t cap_early, int64_t early_layers, const int64_t* __restrict__ tok,
+                  const int64_t* __restrict__ key, const RT* __restrict__ R, int64_t n_r, int64_t r_stride,
+                  const int32_t* __restrict__ bulk_vidx, const int64_t* __restrict__ res_s,
+                  const int64_t* __restrict__ res_seed, const float* __restrict__ E, Lists o) {
+  const int lane = threadIdx.x & 31;
+  const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t l = blockIdx.y;
+  if (!((mode_mask >> l) & 1)) return;  // uniform per CTA
+  const int64_t cap = l < early_layers ? cap_early : cap_main;
+  if ((int64_t)count[l] > cap) return;  // overflowed: this layer went through the dense path
+  const bool ok = col < D;
+  float e[2][kAdmB];
+  int64_t thr[2][kAdmB];
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const float s = p ? -h : h;
-          const int64_t g = (l * 2 + p) * D + col;
-          const int b = bin_of(s, E + g * B, (int)B);
-          if (b >= 0) {
-            const int64_t gr = g * B + b;
-            int64_t thr = res_s[gr * Kr + (Kr - 1)];
-            const int64_t sd = res_seed[gr];
-            if (sd > thr) thr = sd;
-            if (-ky > thr) {
-              rg[nr] = (int32_t)gr; rsc[nr] = -ky; rt[nr] = tk; rv[nr] = h; ++nr;
-            }
-          }
+  for (int p = 0; p < 2; ++p) {
+    const int64_t g = (l * 2 + p) * D + (ok ? col : 0);
+#pragma unroll
+    for (int b = 0; b < kAdmB; ++b) {
+      e[p][b] = (ok && b < B) ? E[g * B + b] : __int_as_float(0x7F800000);  // +inf: never reached
+      int64_t t = INT64_MAX;
+      if (ok && b < B) {
+        const int64_t gr = g * B + b;
+        t = res_s[gr * Kr + (Kr - 1)];
+        const int64_t sd = res_seed[gr];
+        if (sd > t) t = sd;
+      }
+      thr[p][b] = t;
+    }
+  }
+  const int64_t i0 = (int64_t)blockIdx.z * kAdmRows, i1 = i0 + kAdmRows < n_r ? i0 + kAdmRows : n_r;
+#pragma unroll 4
+  for (int64_t i = i0; i < i1; ++i) {  // warp-uniform loop: every lane takes part in the appends
+    int nr = 0;
+    int32_t rg[2];
+    int64_t rsc[2], rt[2];
+    float rv[2];
+    const int32_t vi = bulk_vidx[i];
+    const int64_t ky = key[vi];
+    if (ok) {
+      const float h = ld_elem<RT>(R + (l * r_stride + i) * D + col);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const float s = p ? -h : h;
+        int b = -1;
+#pragma unroll
+        for (int q = 0; q < kAdmB; ++q) b += (q < B && s >= e[p][q]) ? 1 : 0;
+        int64_t t = INT64_MAX;
+#pragma unroll
+        for (int q = 0; q < kAdmB; ++q)
+          if (q == b) t = thr[p][q];
+        if (b >= 0 && -ky > t) {
+          rg[nr] = (int32_t)((((l * 2 + p) * D + col) * B) + b);
+          rsc[nr] = -ky;
+          rt[nr] = tok[vi];
+          rv[nr] = h;
+          ++nr;
         }
       }
-      warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
     }
+    warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
   }
 }
 
@@ -163,7 +205,8 @@ extern "C" int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t K
                 "admit: null reservoir pointer");
   ATLAS_REQUIRE(!reservoir || n_r == 0 || (R && bulk_vidx), "admit: bulk rows missing");
   Lists o{top_g, top_sc, top_tok, top_val, n_top, top_cap, res_g, res_sc, res_tok, res_val, n_res, res_cap, err};
-  const int64_t work = (cap_main > cap_early ? cap_main : cap_early) + n_r * D;
+  ATLAS_REQUIRE(B <= kAdmB, "admit: at most %d bins", kAdmB);
+  const int64_t work = cap_main > cap_early ? cap_main : cap_early;
   const unsigned grid = grid_for(work, 256, 8);
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
@@ -185,5 +228,23 @@ extern "C" int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t K
     default:
       return fail(ATLAS_ERR_ARG, "admit: unknown dtype %d", dtype);
   }
-  return check_launch("atlas_admit");
+  if (int e = check_launch("atlas_admit")) return e;
+  if (!reservoir || n_r == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(L < 65536 && (n_r + kAdmRows - 1) / kAdmRows < 65536, "admit: too many layers or bulk rows");
+  const dim3 gb((unsigned)((D + 255) / 256), (unsigned)L, (unsigned)((n_r + kAdmRows - 1) / kAdmRows));
+  switch (dtype) {
+    case ATLAS_BF16:
+      admit_bulk_kernel<__nv_bfloat16><<<gb, 256, 0, st>>>(L, D, (int)B, Kr, mask, count, cap_main, cap_early,
+          early_layers, tok, key, (const __nv_bfloat16*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, o);
+      break;
+    case ATLAS_F16:
+      admit_bulk_kernel<__half><<<gb, 256, 0, st>>>(L, D, (int)B, Kr, mask, count, cap_main, cap_early, early_layers,
+          tok, key, (const __half*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, o);
+      break;
+    default:
+      admit_bulk_kernel<float><<<gb, 256, 0, st>>>(L, D, (int)B, Kr, mask, count, cap_main, cap_early, early_layers,
+          tok, key, (const float*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, o);
+      break;
+  }
+  return check_launch("atlas_admit: bulk rows");
 }
