@@ -103,78 +103,122 @@ admit_kernel(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t U_r
   }
 }
 
-// Bulk rows (key < U_res; every element is a reservoir candidate), one thread per (layer, column,
-// chunk of kAdmRows rows): the column's bin edges and reservoir thresholds (max of the Kr-th state
-// key and the seed) of both poles are loaded once into registers, then the thread walks its rows
-// (R read coalesced along the columns, the row's key broadcast). Loading the thresholds per element instead
-// made every element fetch a scattered 8-byte slot per pole.
+// Bulk rows (key < U_res; every element is a reservoir candidate). A CTA takes one layer, 256
+// columns and a chunk of up to kAdmRows rows. It first loads its columns' reservoir thresholds
+// (max of the Kr-th state key and the seed, both poles, every bin) into a shared-memory table and
+// the chunk's row keys into shared memory; each thread then holds one column's bin edges in
+// registers and walks the rows (R read coalesced along the columns). Fetching the threshold of
+// each element from global memory instead costs a scattered 8-byte read per element and pole (a
+// 32-byte sector per lane), which dominated the admission time.
 constexpr int kAdmB = 8;
-constexpr int kAdmRows = 16;  // bulk rows per CTA (grid z): enough CTAs even for one layer
+constexpr int kAdmRows = 64;  // most bulk rows per CTA (grid z); fewer when that leaves the GPU short of CTAs
+constexpr int kAdmCols = 256;
 
-template <typename RT>
-__global__ void __launch_bounds__(256)
-admit_bulk_kernel(int64_t L, int64_t D, int B, int64_t Kr, uint64_t mode_mask, const int32_t* __restrict__ count,
+template <typename RT, int NB>
+__global__ void __launch_bounds__(kAdmCols)
+admit_bulk_kernel(int64_t L, int64_t D, int64_t Kr, uint64_t mode_mask, const int32_t* __restrict__ count,
                   int64_t cap_main, int64_t cap_early, int64_t early_layers, const int64_t* __restrict__ tok,
                   const int64_t* __restrict__ key, const RT* __restrict__ R, int64_t n_r, int64_t r_stride,
                   const int32_t* __restrict__ bulk_vidx, const int64_t* __restrict__ res_s,
-                  const int64_t* __restrict__ res_seed, const float* __restrict__ E, Lists o) {
+                  const int64_t* __restrict__ res_seed, const float* __restrict__ E, int rows_per_cta, Lists o) {
   const int lane = threadIdx.x & 31;
-  const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t col = (int64_t)blockIdx.x * kAdmCols + threadIdx.x;
   const int64_t l = blockIdx.y;
   if (!((mode_mask >> l) & 1)) return;  // uniform per CTA
   const int64_t cap = l < early_layers ? cap_early : cap_main;
   if ((int64_t)count[l] > cap) return;  // overflowed: this layer went through the dense path
+  __shared__ int64_t s_thr[2][NB][kAdmCols];
+  __shared__ int64_t s_key[kAdmRows];
+  __shared__ int32_t s_vi[kAdmRows];
   const bool ok = col < D;
-  float e[2][kAdmB];
-  int64_t thr[2][kAdmB];
+  const int64_t i0 = (int64_t)blockIdx.z * rows_per_cta;  // rows_per_cta <= kAdmRows
+  const int nrows = (int)(i0 + rows_per_cta < n_r ? rows_per_cta : n_r - i0);
+  float e[2][NB];
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const int64_t g = (l * 2 + p) * D + (ok ? col : 0);
 #pragma unroll
-    for (int b = 0; b < kAdmB; ++b) {
-      e[p][b] = (ok && b < B) ? E[g * B + b] : __int_as_float(0x7F800000);  // +inf: never reached
+    for (int b = 0; b < NB; ++b) {
+      e[p][b] = ok ? E[g * NB + b] : __int_as_float(0x7F800000);  // +inf: never reached
       int64_t t = INT64_MAX;
-      if (ok && b < B) {
-        const int64_t gr = g * B + b;
+      if (ok) {
+        const int64_t gr = g * NB + b;
         t = res_s[gr * Kr + (Kr - 1)];
         const int64_t sd = res_seed[gr];
         if (sd > t) t = sd;
       }
-      thr[p][b] = t;
+      s_thr[p][b][threadIdx.x] = t;
     }
   }
-  const int64_t i0 = (int64_t)blockIdx.z * kAdmRows, i1 = i0 + kAdmRows < n_r ? i0 + kAdmRows : n_r;
-#pragma unroll 4
-  for (int64_t i = i0; i < i1; ++i) {  // warp-uniform loop: every lane takes part in the appends
+  if (threadIdx.x < nrows) {
+    const int32_t vi = bulk_vidx[i0 + threadIdx.x];
+    s_vi[threadIdx.x] = vi;
+    s_key[threadIdx.x] = key[vi];
+  }
+  __syncthreads();
+  const RT* Rc = R + (l * r_stride + i0) * D + col;  // this column, first row of the chunk
+  for (int r0 = 0; r0 < nrows; r0 += 8) {  // warp-uniform: every lane takes part in the appends
+    float hv[8];  // eight rows' values in flight before any compare
+#pragma unroll
+    for (int u = 0; u < 8; ++u) hv[u] = (ok && r0 + u < nrows) ? ld_elem<RT>(Rc + (int64_t)(r0 + u) * D) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+    const int r = r0 + u;
+    if (r >= nrows) break;
     int nr = 0;
     int32_t rg[2];
     int64_t rsc[2], rt[2];
     float rv[2];
-    const int32_t vi = bulk_vidx[i];
-    const int64_t ky = key[vi];
+    const int64_t ky = s_key[r];
     if (ok) {
-      const float h = ld_elem<RT>(R + (l * r_stride + i) * D + col);
+      const float h = hv[u];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const float s = p ? -h : h;
         int b = -1;
 #pragma unroll
-        for (int q = 0; q < kAdmB; ++q) b += (q < B && s >= e[p][q]) ? 1 : 0;
-        int64_t t = INT64_MAX;
-#pragma unroll
-        for (int q = 0; q < kAdmB; ++q)
-          if (q == b) t = thr[p][q];
-        if (b >= 0 && -ky > t) {
-          rg[nr] = (int32_t)((((l * 2 + p) * D + col) * B) + b);
+        for (int q = 0; q < NB; ++q) b += (s >= e[p][q]) ? 1 : 0;
+        if (b >= 0 && -ky > s_thr[p][b][threadIdx.x]) {
+          rg[nr] = (int32_t)((((l * 2 + p) * D + col) * NB) + b);
           rsc[nr] = -ky;
-          rt[nr] = tok[vi];
+          rt[nr] = tok[s_vi[r]];
           rv[nr] = h;
           ++nr;
         }
       }
     }
     warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
+    }
   }
+}
+
+template <typename RT, int NB>
+void launch_admit_bulk(dim3 gb, cudaStream_t st, int64_t L, int64_t D, int64_t Kr, uint64_t mask, const int32_t* count,
+                       int64_t cap_main, int64_t cap_early, int64_t early_layers, const int64_t* tok, const int64_t* key,
+                       const void* R, int64_t n_r, int64_t r_stride, const int32_t* bulk_vidx, const int64_t* res_s,
+                       const int64_t* res_seed, const float* E, int rows_per_cta, Lists o) {
+  admit_bulk_kernel<RT, NB><<<gb, kAdmCols, 0, st>>>(L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key,
+                                                    (const RT*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E,
+                                                    rows_per_cta, o);
+}
+
+template <typename RT>
+int launch_admit_bulk_b(int64_t B, dim3 gb, cudaStream_t st, int64_t L, int64_t D, int64_t Kr, uint64_t mask,
+                        const int32_t* count, int64_t cap_main, int64_t cap_early, int64_t early_layers,
+                        const int64_t* tok, const int64_t* key, const void* R, int64_t n_r, int64_t r_stride,
+                        const int32_t* bulk_vidx, const int64_t* res_s, const int64_t* res_seed, const float* E,
+                        int rows_per_cta, Lists o) {
+#define ATLAS_ADMIT_B(NBV)                                                                                           \
+  case NBV:                                                                                                         \
+    launch_admit_bulk<RT, NBV>(gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key, R, n_r,  \
+                               r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);                           \
+    return ATLAS_OK;
+  switch (B) {
+    ATLAS_ADMIT_B(1) ATLAS_ADMIT_B(2) ATLAS_ADMIT_B(3) ATLAS_ADMIT_B(4)
+    ATLAS_ADMIT_B(5) ATLAS_ADMIT_B(6) ATLAS_ADMIT_B(7) ATLAS_ADMIT_B(8)
+    default: return fail(ATLAS_ERR_ARG, "admit: B must be 1..%d", kAdmB);
+  }
+#undef ATLAS_ADMIT_B
 }
 
 }  // namespace
@@ -230,21 +274,29 @@ extern "C" int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t K
   }
   if (int e = check_launch("atlas_admit")) return e;
   if (!reservoir || n_r == 0) return ATLAS_OK;
-  ATLAS_REQUIRE(L < 65536 && (n_r + kAdmRows - 1) / kAdmRows < 65536, "admit: too many layers or bulk rows");
-  const dim3 gb((unsigned)((D + 255) / 256), (unsigned)L, (unsigned)((n_r + kAdmRows - 1) / kAdmRows));
+  // rows per CTA: up to kAdmRows (the column's thresholds are loaded once per CTA), but at least about
+  // one wave of CTAs (8 per SM) when the batch has few layers or bulk rows
+  const int64_t col_blocks = (D + kAdmCols - 1) / kAdmCols;
+  int64_t rpc = (n_r * col_blocks * L + (int64_t)num_sms() * 8 - 1) / ((int64_t)num_sms() * 8);
+  rpc = rpc < 8 ? 8 : (rpc > kAdmRows ? kAdmRows : rpc);
+  ATLAS_REQUIRE(L < 65536 && (n_r + rpc - 1) / rpc < 65536, "admit: too many layers or bulk rows");
+  const dim3 gb((unsigned)col_blocks, (unsigned)L, (unsigned)((n_r + rpc - 1) / rpc));
+  const int rows_per_cta = (int)rpc;
+  int e2;
   switch (dtype) {
     case ATLAS_BF16:
-      admit_bulk_kernel<__nv_bfloat16><<<gb, 256, 0, st>>>(L, D, (int)B, Kr, mask, count, cap_main, cap_early,
-          early_layers, tok, key, (const __nv_bfloat16*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, o);
+      e2 = launch_admit_bulk_b<__nv_bfloat16>(B, gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok,
+                                              key, R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);
       break;
     case ATLAS_F16:
-      admit_bulk_kernel<__half><<<gb, 256, 0, st>>>(L, D, (int)B, Kr, mask, count, cap_main, cap_early, early_layers,
-          tok, key, (const __half*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, o);
+      e2 = launch_admit_bulk_b<__half>(B, gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key, R,
+                                       n_r, r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);
       break;
     default:
-      admit_bulk_kernel<float><<<gb, 256, 0, st>>>(L, D, (int)B, Kr, mask, count, cap_main, cap_early, early_layers,
-          tok, key, (const float*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, o);
+      e2 = launch_admit_bulk_b<float>(B, gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key, R,
+                                      n_r, r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);
       break;
   }
+  if (e2) return e2;
   return check_launch("atlas_admit: bulk rows");
 }
