@@ -51,6 +51,22 @@ def _shard(z, h):
     return a
 
 
+def _empty_shard(z):
+    """A rank that streamed nothing: the same edges, seeds and config, empty state."""
+    a = _shard(z, 0)
+    a.top_k.fill_(torch.iinfo(torch.int64).min)
+    a.top_t.fill_(-1)
+    a.top_s.fill_(float("-inf"))
+    a.res_s.fill_(torch.iinfo(torch.int64).min)
+    a.res_t.fill_(-1)
+    a.res_v.fill_(float("nan"))
+    for k in ("sub_sum", "sub_sq", "sub_bin", "enr", "ann_tot"):
+        getattr(a, k).zero_()
+    a.n_seen = a.n_sub = 0
+    a.stats = {"batches": 0}
+    return a
+
+
 def _worker(rank, world, port, mode, q):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -61,7 +77,7 @@ def _worker(rank, world, port, mode, q):
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure before the combine")
         z = golden("merge_from")
-        a = _shard(z, rank)
+        a = _shard(z, rank) if rank < 2 else _empty_shard(z)
         warm_up()
         merge_states(a, row_merge=cpu_row_merge, gram=False)
         want = {k[2:]: v for k, v in z.items() if k.startswith("m_")}
@@ -85,11 +101,11 @@ def _worker(rank, world, port, mode, q):
         q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-400:]}"))
 
 
-def _run(mode, timeout=120):
+def _run(mode, timeout=120, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in ps:
         p.start()
     out = {}
@@ -108,6 +124,15 @@ def test_merge_states_two_ranks_matches_reference():
     for r in (0, 1):
         assert isinstance(out[r], dict), out[r]
         assert all(out[r].values()), out[r]
+
+
+def test_merge_states_five_ranks_uneven_slices_matches_reference():
+    """World size 5: the 2*2*48 = 192 group rows do not divide by 5, so the all-to-all slices are
+    padded; ranks 2-4 streamed nothing. Every rank must still end with the reference's merged state."""
+    out = _run("ok", world=5, timeout=180)
+    for r in range(5):
+        assert isinstance(out[r], dict), out[r]
+        assert all(out[r].values()), (r, out[r])
 
 
 def test_failed_rank_ends_combine_with_error_not_hang():
