@@ -445,22 +445,47 @@ def c2_stream(dev, peaks, scale, shift, n_blocks=64, warm=8, T=16384, D=5120):
     return res
 
 
-# ----------------------------------------------------------------------------- CPU side (oracle)
-def cpu_sample_stream(n_batches, layers, seed, T=32768, D=D_650M):
-    """Synthetic activation blocks with the C4 layer shape and a heavy-tailed value distribution
-    (Student-t nu=3 x per-column scale + shift), 8% padding rows, tokens seq*1024+pos."""
-    rng = np.random.default_rng(seed)
-    scale = (rng.random((layers, D)) * 1.5 + 0.5).astype(np.float32)
-    shift = (rng.standard_normal((layers, D)) * 0.5).astype(np.float32)
+# ----------------------------------------------------------------------------- CPU side (reference, oracle)
+def host_cores() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+CPU_LMAX = 300
+CPU_T = (32768 // CPU_LMAX) * CPU_LMAX  # padded rows of a CPU sample batch (109 sequences x 300)
+
+
+def cpu_sample_batches(n_batches, seed, T=CPU_T, Lmax=CPU_LMAX):
+    """Row layout of C4-like batches: [T] padded rows of sequences of length <= Lmax - 2 (rows
+    r*Lmax + 1 + pos), tokens seq*1024 + pos, annotation = residue class (21 classes)."""
     out = []
+    nseq = T // Lmax
     for bi in range(n_batches):
-        Lmax = 300
-        nseq = T // Lmax
-        valid = np.concatenate([r * Lmax + 1 + np.arange(Lmax - 2 - (r % 17)) for r in range(nseq)])
-        tok = np.concatenate([(bi * nseq + r) * 1024 + np.arange(Lmax - 2 - (r % 17)) for r in range(nseq)])
-        Hs = [(rng.standard_t(3, (nseq * Lmax, D)).astype(np.float32) * scale[l] + shift[l]) for l in range(layers)]
+        lens = [Lmax - 2 - ((r + bi) % 17) for r in range(nseq)]
+        valid = np.concatenate([r * Lmax + 1 + np.arange(n) for r, n in enumerate(lens)]).astype(np.int64)
+        tok = np.concatenate([(bi * nseq + r) * 1024 + np.arange(n) for r, n in enumerate(lens)]).astype(np.int64)
         ann = (tok % 21)[:, None].astype(np.int64)
-        out.append((nseq * Lmax, valid.astype(np.int64), tok.astype(np.int64), ann, Hs))
+        out.append((nseq * Lmax, valid, tok, ann))
+    return out
+
+
+def cpu_sample_blocks(n_blocks, seed, T=CPU_T, D=D_650M):
+    """Activation blocks [T, D] bf16 of the C4 layer shape: Student-t(3) (a normal over the root of a
+    chi-square of three normals / 3) x per-column scale U(0.5, 2) + per-column shift N(0, 0.5), the
+    scale and shift of block j from cpu_sample_seeds' law for layer j."""
+    rng = np.random.default_rng(seed)
+    scale = (rng.random((n_blocks, D)) * 1.5 + 0.5).astype(np.float32)
+    shift = (rng.standard_normal((n_blocks, D)) * 0.5).astype(np.float32)
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for j in range(n_blocks):
+        h = torch.randn(T, D, generator=g)
+        c = torch.zeros(T, D)
+        for _ in range(3):
+            z = torch.randn(T, D, generator=g)
+            c.addcmul_(z, z)
+        h.div_(c.div_(3.0).sqrt_()).mul_(torch.from_numpy(scale[j])).add_(torch.from_numpy(shift[j]))
+        out.append(h.to(torch.bfloat16))
+        del h, c
     return out
 
 
@@ -486,29 +511,76 @@ def cpu_sample_seeds(layers, seed, K=100, Kr=32, pilot_tokens=660_000, n_total=1
     return E, top, rk
 
 
-def cpu_oracle_run(steps, warmup, layers=1, seed=11):
-    """Time the numpy oracle (reference algorithm, stats v1 + merge loop) on `layers` layers of the
-    C4 shape in the seeded steady state; returns tokens/s for the full 33-layer atlas."""
+def reference_cpu_run(steps, warmup, layers=4, seed=11, blocks=None):
+    """Time the reference's own CPU implementation of the path: its Atlas(backend="torch",
+    stats_impl="v1", merge_impl="loop", device="cpu") from the compiled reference (oracle/_ref), on
+    every host core, seeded, in the stream's steady state, over `layers` of the 33 C4 layers (each
+    fed its own [32768 x 5120] bf16 activation block). A step is one batch: begin_batch, observe on
+    every sampled layer, end_batch (with the reference's dense redo when it asks for one), timed
+    with perf_counter as the reference's own driver brackets it; make_ctx runs before the clock (the
+    reference builds it on a prefetch thread). tokens/s = valid tokens / (time per layer x 33).
+    Raises oracle.build_ref.ReferenceUnavailable when oracle/_ref was not built."""
+    from oracle.build_ref import load_reference_atlas
+    rc = load_reference_atlas()
+    cores = host_cores()
+    torch.set_num_threads(cores)
+    blocks = blocks if blocks is not None else cpu_sample_blocks(layers, seed)
+    E, ts, rk = cpu_sample_seeds(layers, seed)
+    cfg = rc.AtlasConfig(K=100, Kr=32, seed=0, backend="torch", stats_impl="v1", merge_impl="loop")
+    at = rc.Atlas(layers, D_650M, torch.from_numpy(E), cfg, n_annot=21, device="cpu")
+    at.seed(torch.from_numpy(ts), torch.from_numpy(rk))
+    times, toks, redo_n = [], [], 0
+    with torch.no_grad():
+        for i, (T, valid, tok, ann) in enumerate(cpu_sample_batches(warmup + steps, seed)):
+            ctx = at.make_ctx(T, torch.from_numpy(valid), torch.from_numpy(tok), torch.from_numpy(ann), device="cpu")
+            t0 = time.perf_counter()
+            at.begin_batch(ctx)
+            for l in range(layers):
+                at.observe(l, blocks[l])
+            redo = at.end_batch()
+            if redo:
+                redo_n += len(redo)
+                at.begin_batch(ctx, redo_layers=redo)
+                for l in redo:
+                    at.observe(l, blocks[l])
+                at.end_batch()
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times.append(dt)
+                toks.append(valid.size)
+    per_tok_layer = sum(times) / (sum(toks) * layers)
+    value = 1.0 / (per_tok_layer * L_650M)
+    sample = (f"the reference's own CPU implementation, compiled from its atlas package into oracle/_ref: "
+              f"Atlas(backend='torch', stats_impl='v1', merge_impl='loop', device='cpu'), {cores} threads; "
+              f"{len(times)} timed batches (+{warmup} warm-up) x {layers} of the 33 C4 layers, each a [32768 x 5120] "
+              f"bf16 synthetic heavy-tailed activation block, K=100 Kr=32, 5 bins, seeded steady state; time per "
+              f"layer-batch extrapolated to 33 layers; dense redo layer-batches {redo_n}; forward not included")
+    return value, sample, cores, times
+
+
+def cpu_oracle_run(steps, warmup, layers=1, seed=11, blocks=None):
+    """Time the numpy oracle (the CPU restatement of the reference algorithm, stats v1 + merge loop)
+    on `layers` layers of the C4 shape in the seeded steady state; tokens/s for the 33-layer atlas."""
     from oracle import atlas_np as O
     # every host core, whatever torchrun set OMP_NUM_THREADS to (it sets 1 per rank): the oracle's
     # thread pool and numpy's BLAS both get the whole affinity set
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    cores = host_cores()
     os.environ["ORACLE_THREADS"] = str(cores)
     try:
         from threadpoolctl import threadpool_limits
         blas = threadpool_limits(limits=cores)
     except Exception:  # noqa: BLE001  threadpoolctl missing: numpy keeps its own setting
         blas = None
-    n_b = warmup + steps
-    data = cpu_sample_stream(n_b, layers, seed)
+    blocks = blocks if blocks is not None else cpu_sample_blocks(layers, seed)
+    Hs = [b.float().numpy() for b in blocks[:layers]]
     E, ts, rk = cpu_sample_seeds(layers, seed)
     cfg = O.OracleConfig(K=100, Kr=32, seed=0)
     at = O.AtlasOracle(layers, D_650M, E, cfg, n_annot=21)
     at.seed(ts, rk)
     times, toks = [], []
-    for i, (T, valid, tok, ann, Hs) in enumerate(data):
-        t0 = time.perf_counter()
+    for i, (T, valid, tok, ann) in enumerate(cpu_sample_batches(warmup + steps, seed)):
         ctx = at.make_ctx(T, valid, tok, ann)
+        t0 = time.perf_counter()
         at.begin_batch(ctx)
         for l in range(layers):
             at.observe(l, Hs[l])
@@ -524,13 +596,27 @@ def cpu_oracle_run(steps, warmup, layers=1, seed=11):
             toks.append(valid.size)
     per_tok_layer = sum(times) / (sum(toks) * layers)
     value = 1.0 / (per_tok_layer * L_650M)
-    threads = cores
     if blas is not None:
         blas.restore_original_limits()
-    sample = (f"numpy oracle of the reference atlas (stats v1, merge loop), {len(times)} batches x {layers} of 33 "
-              f"layers, [32768 x 5120] synthetic heavy-tailed activations, K=100 Kr=32, seeded; extrapolated to 33 "
-              f"layers; forward not included")
-    return value, sample, threads, times
+    sample = (f"numpy restatement of the reference atlas (oracle/atlas_np.py; stats v1, merge loop), {cores} threads, "
+              f"{len(times)} batches x {layers} of 33 layers, [32768 x 5120] synthetic heavy-tailed activations, "
+              f"K=100 Kr=32, seeded; extrapolated to 33 layers; forward not included")
+    return value, sample, cores, times
+
+
+def cpu_baselines(steps, warmup, layers=4):
+    """The reference's own CPU path (kind "reference") when oracle/_ref is built, plus the numpy port
+    as a second, labelled figure; the port alone (kind "port") otherwise."""
+    from oracle.build_ref import ReferenceUnavailable
+    blocks = cpu_sample_blocks(layers, 11)
+    port_v, port_s, port_c, _ = cpu_oracle_run(max(1, steps - 1), 1, layers=1, blocks=blocks)
+    port = {"value": port_v, "unit": "tokens/s", "cores": port_c, "kind": "port", "sample": port_s}
+    try:
+        v, sample, cores, _ = reference_cpu_run(steps, warmup, layers=layers, blocks=blocks)
+    except ReferenceUnavailable as e:
+        port["note"] = f"reference arm unavailable: {e}"
+        return port, None
+    return {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample}, port
 
 
 # ----------------------------------------------------------------------------- main
@@ -564,13 +650,22 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return
-        value, sample, threads, _ = cpu_oracle_run(args.steps if args.steps <= 5 else 5, 1)
+        from oracle.build_ref import ReferenceUnavailable
+        # a step is one batch over a sample of the 33 layers, sized so that the whole --steps/--warmup
+        # run stays within a few minutes on the host cores
+        layers = int(os.environ.get("PROTEUS_REF_LAYERS", "4"))
+        try:
+            value, sample, threads, _ = reference_cpu_run(args.steps, args.warmup, layers=layers)
+            kind, path = "reference", "the reference's own Atlas (torch, v1, loop) on CPU, compiled into oracle/_ref"
+        except ReferenceUnavailable as e:
+            value, sample, threads, _ = cpu_oracle_run(min(args.steps, 5), 1)
+            kind, path = "port", f"CPU restatement (oracle/atlas_np.py); compiled reference unavailable: {e}"
         cfg = {"workload": "C4: ESM-2 650M (33 x 5120 units x 2 poles) streaming atlas, K=100, Kr=32, 5 bins, seeded",
-               "tokens_per_batch": args.tokens_per_batch, "reference_path": "CPU restatement (oracle/atlas_np.py)"}
+               "tokens_per_batch": args.tokens_per_batch, "reference_path": path}
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
-                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind, "sample": sample},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -748,8 +843,10 @@ def main():
         if not args.no_micro:
             line["kernels"] = kernel_microbench(dev, peaks)
         if not args.no_cpu:
-            v, sample, threads, _ = cpu_oracle_run(args.cpu_steps, 1)
-            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+            base, port = cpu_baselines(args.cpu_steps, 1)
+            line["cpu_baseline"] = base
+            if port is not None:
+                line["cpu_baseline_port"] = port
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

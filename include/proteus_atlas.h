@@ -37,6 +37,10 @@ enum atlas_status {
  * the failure here and finishes). Synchronous read; `reset` clears it. No counterpart in the
  * reference (its Triton kernels have no waits). */
 int atlas_device_status(int* status_host, int reset);
+/* Test hook: writes `code` into the device status word (synchronous), so that a host can exercise
+ * its handling of a failed wait (refusing results and checkpoints) without making a wait give up.
+ * No counterpart in the reference. */
+int atlas_device_status_set(int code);
 
 /* Message of the last error raised on the calling host thread ("" if none). */
 const char* atlas_last_error(void);
@@ -82,7 +86,7 @@ int atlas_gather_rows(const void* H, int dtype, int64_t T, int64_t D, int64_t ld
                       int64_t n, void* R, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
- * Subsample statistics — replaces sub_stats (atlas/stats_triton.py:163-203) and the accumulation
+ * Subsample statistics — replaces sub_stats (atlas/stats_triton.py:77-117) and the accumulation
  * of Atlas._subsample_stats_v3 / _v1 (atlas/core.py:312-338, :378-399).
  * Input XT [D, n] (columns col0..col0+n of a transposed staging buffer, leading dim ldx).
  * Accumulates in place, per column d:
@@ -108,7 +112,7 @@ int atlas_count_gemm_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int
 
 /* ------------------------------------------------------------------------------------------------
  * Upper-block-triangle Gram on tcgen05 tensor cores — replaces gram_accumulate
- * (atlas/stats_triton.py:234-255): C[D, D] (fp32, row-major, contiguous) += X^T X on the 128x128
+ * (atlas/stats_triton.py:148-169): C[D, D] (fp32, row-major, contiguous) += X^T X on the 128x128
  * blocks with block row <= block column; lower blocks untouched. X is supplied transposed:
  * XT [D, n] bf16 or fp16 (tcgen05, fp32 accumulation) or fp32 (exact fp32 FMA on CUDA cores) with
  * leading dimension ldx (elements; ldx % 8 == 0, 16-byte aligned base).
@@ -196,11 +200,14 @@ int atlas_grouped_merge(int64_t* state_sc, int64_t* state_tok, float* state_val,
  * every device byte through its own pool and forbids side allocations, or a call site that must not
  * pay for cudaMalloc's implicit device synchronisation in the middle of a stream.
  * Limits: G <= 262144 groups and n_max <= 262144 records per call (larger requests are rejected
- * with ATLAS_ERR_ARG); the array (about 11 MB) stays resident on every GPU that loads the library
- * until the process exits. The first call on a device looks up the array's device address (make it
- * before any stream capture on that device). All calls share the one array: calls that can overlap
- * on the GPU (different streams, or devices sharing nothing but this library) race and must be
- * serialised by the caller. Nothing is allocated, by this call or by anything it calls.
+ * with ATLAS_ERR_ARG). Each GPU has its own copy of the array (about 11 MB). It is created when the
+ * library's device code is first loaded on that GPU (under lazy module loading, the CUDA default,
+ * that is this entry point's first call there) and stays until the process exits. Make one warm-up
+ * call per GPU at initialisation, before any stream capture on it. Calls on one GPU share its copy:
+ * calls on that GPU that can overlap (different streams, or several host threads) race and must be
+ * serialised by the caller; calls on different GPUs do not race. The library must not be used across
+ * a cudaDeviceReset of the calling context's device while a call is in flight. Nothing is allocated
+ * by this call or by anything it calls beyond that one array.
  */
 int atlas_grouped_merge_static(int64_t* state_sc, int64_t* state_tok, float* state_val, int64_t G, int64_t K,
                                const int32_t* g, const int64_t* sc, const int64_t* tok, const float* val,

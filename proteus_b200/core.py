@@ -358,7 +358,7 @@ class Atlas:
         self._stats["elements"] += 2 * ctx.n_v * self.D * self.L
         self._ensure_buffers(ctx)
         self._counts.zero_()
-        self._flags.zero_()
+        self._flags[:self.L + 2].zero_()  # the list-overflow flag (slot L + 2) stays set once raised
         c = self.cfg
         call("atlas_thresholds", ptr(self.top_s), c.K, ptr(self.res_s), c.Kr, ptr(self.top_seed), ptr(self.res_seed),
              ptr(self.E), self.L * 2 * self.D, self.B, self.U_res, int(bool(c.reservoir)), ptr(self.thr),
@@ -556,11 +556,27 @@ class Atlas:
         call("atlas_batch_counters", ptr(self._counts), L, fmask.data_ptr(), cap_main, cap_early, early,
              ptr(fl[L:L + 1]), ptr(fl[L + 1:L + 2]), ptr(self._dev_stats), stream_ptr(self.dev))
 
+    def device_status(self) -> int:
+        """Status word of the bounded device waits on this atlas's GPU: 0, or the code of the first
+        wait (tcgen05 / TMA mbarrier) that gave up; that launch's output is then incomplete."""
+        import ctypes
+        v = ctypes.c_int(0)
+        with torch.cuda.device(self.dev):
+            call("atlas_device_status", ctypes.byref(v), 0)
+        return int(v.value)
+
     def check_errors(self):
-        """Raise if a device-side list ran out of capacity (never expected: lists are sized for the
-        worst case of the batch)."""
+        """Raise if the device recorded anything that invalidates the state: a record list that ran
+        out of capacity (the flag is sticky from the batch that overflowed it; never expected, the
+        lists are sized for each batch's worst case), or a bounded wait that gave up. One
+        synchronisation. state_dict() and result() call it, so a flagged state is never written to
+        a checkpoint or returned."""
         if int(self._flags[self.L + 2]):
-            raise AtlasKernelError("a candidate list overflowed its capacity")
+            raise AtlasKernelError("a candidate record list overflowed its capacity: this atlas state is incomplete")
+        st = self.device_status()
+        if st:
+            raise AtlasKernelError(f"device status {st}: a bounded wait of a tensor-core or TMA kernel gave up, "
+                                   "so its output is incomplete: this atlas state is invalid")
 
     # ------------------------------------------------------------------ outputs
     def flush_gram(self):
@@ -574,7 +590,9 @@ class Atlas:
               "top_seed", "res_seed"]
 
     def state_dict(self) -> dict:
-        """Checkpoint dict in the reference's format (core.py:605-614); CPU tensors, no Gram."""
+        """Checkpoint dict in the reference's format (core.py:605-614); CPU tensors, no Gram.
+        Raises (check_errors) instead of returning a state the device flagged as incomplete."""
+        self.check_errors()
         st = {k: getattr(self, k).cpu() for k in self._STATE}
         if self.n_a:
             st["enr"], st["ann_tot"] = self.enr.cpu(), self.ann_tot.cpu()
@@ -631,6 +649,7 @@ class Atlas:
         """Final views and checks (core.py:656-676)."""
         L, D, B, K, Kr = self.L, self.D, self.B, self.cfg.K, self.cfg.Kr
         self.flush_gram()
+        self.check_errors()
         top_s = self.top_s.view(L, 2, D, K).cpu()
         sign = torch.tensor([1.0, -1.0]).view(1, 2, 1, 1)
         out = {

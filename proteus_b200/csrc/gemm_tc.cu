@@ -3,7 +3,7 @@
 //   allocation), warps 2-5: epilogue (TMEM -> registers -> global), one thread per accumulator row.
 //
 // atlas_gram_upper  C[D, D] += X^T X on the upper 128-block triangle (gram_accumulate,
-//                   stats_triton.py:234-255). One CTA per 128x128 output block; bf16/fp16 operands
+//                   stats_triton.py:148-169). One CTA per 128x128 output block; bf16/fp16 operands
 //                   from the transposed staging XT [D, n] (both operands K-major, 128-byte swizzle);
 //                   fp32 accumulation in TMEM in segments of 1024 rows, double-buffered so the
 //                   epilogue folds a finished segment into register totals while the next one is
@@ -614,6 +614,14 @@ extern "C" int atlas_device_status(int* status_host, int reset) {
   }
   if (atlas::filter_device_status(&vf, reset) != ATLAS_OK) return fail(ATLAS_ERR_CUDA, "device_status: read failed");
   if (status_host) *status_host = v ? v : vf;
+  return ATLAS_OK;
+}
+
+// Writes `code` into this file's status word (synchronous). Lets a host exercise its error path
+// (check_errors, result, checkpoint refusal) without making a device wait give up.
+extern "C" int atlas_device_status_set(int code) {
+  if (cudaMemcpyToSymbol(tc::g_device_status, &code, sizeof(int)) != cudaSuccess)
+    return fail(ATLAS_ERR_CUDA, "device_status_set: write failed");
   return ATLAS_OK;
 }
 

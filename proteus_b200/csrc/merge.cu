@@ -391,23 +391,17 @@ constexpr int64_t kStaticI32Bytes = (kStaticI32 * 4 + 255) / 256 * 256;
 constexpr int64_t kStaticRecBytes = 3 * ((8 * kStaticMergeRecords + 255) / 256 * 256);
 static __device__ __align__(256) unsigned char g_merge_scratch[kStaticI32Bytes + kStaticRecBytes];
 
-// Device address of g_merge_scratch, looked up once per device (host code only holds a stand-in
-// for the symbol, which must never be handed to a kernel).
-constexpr int kMaxDevices = 64;
-static void* g_scratch_addr[kMaxDevices] = {};
-
+// Device address of g_merge_scratch on the current device, looked up on every call (a cheap lookup).
+// It is not cached: after a cudaDeviceReset the module is loaded again and the array can move, so a
+// cached address could point at freed memory. Host code only holds a stand-in for the symbol, which
+// must never be handed to a kernel. Under lazy module loading (the CUDA default) the first lookup on
+// a device is what loads this module there and creates the array.
 int static_scratch(void** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return fail(ATLAS_ERR_CUDA, "grouped_merge_static: no current CUDA device");
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_merge_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(ATLAS_ERR_CUDA, "grouped_merge_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_merge_scratch);
+  if (e != cudaSuccess || !p)
+    return fail(ATLAS_ERR_CUDA, "grouped_merge_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  *out = p;
   return ATLAS_OK;
 }
 }  // namespace

@@ -13,11 +13,15 @@ contract, tests/test_resume_merge.py:56-60; Atlas.merge_from asserts it, atlas/c
     every rank receiving every rank's whole state);
   counts (sub_bin, enr, ann_tot, n_seen, n_sub): all-reduce SUM in int64 (exact);
   moments (sub_sum, sub_sq, fp64): all-gathered and summed in rank order (deterministic);
-  Gram: each rank flushes to fp64 and the fp64 matrices are summed in rank order, layer by layer.
+  Gram: each rank flushes to fp64; layer by layer, an all-to-all sends slice r of every rank's
+    matrix to rank r, which sums the `world` copies in rank order (deterministic, and each rank
+    receives one slice per peer instead of every peer's whole matrix), and an all-gather returns
+    the summed slices to every rank.
+The shards must share edges, config and both seeds: a SHA-256 of their bytes is compared first.
 """
 from __future__ import annotations
 
-import zlib
+import hashlib
 
 import torch
 import torch.distributed as dist
@@ -28,6 +32,30 @@ I64_MIN = torch.iinfo(torch.int64).min
 def shard_plan(plan: list, world: int, rank: int) -> list:
     """Batches of this rank: plan[rank::world] (disjoint, covering, deterministic)."""
     return plan[rank::world]
+
+
+class Lockstep:
+    """Per-batch agreement of the ranks of a sharded stream on how to go on. Each rank proposes a
+    code (0 = continue, larger = stop, e.g. 1 = simulated cap, 2 = deadline: checkpoint and exit)
+    and says whether it has batches left; after `agree` every rank holds the same largest code and
+    knows whether any rank still has work. Ranks whose shard is exhausted keep calling `agree`
+    (without a batch) until every shard is, so all ranks leave the loop at the same step and enter
+    the combine together, and a stop taken by one rank is taken by all. One all-reduce of two ints
+    per batch (a host read: the one synchronisation per batch that the loop already makes)."""
+
+    def __init__(self, group=None, device=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.buf = torch.zeros(2, dtype=torch.int64, device=device if device is not None else "cpu")
+
+    def agree(self, code: int, more: bool) -> tuple[int, bool]:
+        if self.world == 1:
+            return int(code), bool(more)
+        self.buf[0] = int(code)
+        self.buf[1] = int(bool(more))
+        dist.all_reduce(self.buf, op=dist.ReduceOp.MAX, group=self.group)
+        c, m = self.buf.tolist()
+        return int(c), bool(m)
 
 
 def _row_merge_cuda(sc, tok, val, osc, otok, oval):
@@ -72,6 +100,37 @@ def _sum_in_rank_order(t: torch.Tensor, world, group) -> torch.Tensor:
     return acc
 
 
+def _reduce_slices_in_rank_order(t: torch.Tensor, world, group) -> torch.Tensor:
+    """Sum of `t` over the ranks, in rank order, returned on every rank: all-to-all of `world`
+    slices of the flattened tensor, a rank-ordered sum of the copies of the own slice, all-gather
+    of the sums. Per rank it receives about 2x the tensor, against world x for an all-gather of
+    whole tensors, with the same summation order."""
+    n = t.numel()
+    per = -(-n // world)
+    flat = t.reshape(-1)
+    src = flat if per * world == n else torch.cat([flat, flat.new_zeros(per * world - n)])
+    recv = torch.empty_like(src)
+    dist.all_to_all_single(recv, src.contiguous(), group=group)
+    parts = recv.view(world, per)
+    acc = parts[0].clone()
+    for r in range(1, world):
+        acc += parts[r]
+    out = torch.empty_like(src)
+    dist.all_gather_into_tensor(out, acc, group=group)
+    return out[:n].view_as(t)
+
+
+def shard_signature(atlas) -> str:
+    """SHA-256 of the bytes of the edges, both seeds and the config: two shards may be combined only
+    when these are identical (atlas/core.py:632-634)."""
+    h = hashlib.sha256()
+    for t in (atlas.E, atlas.top_seed, atlas.res_seed):
+        h.update(str(tuple(t.shape)).encode())
+        h.update(t.detach().contiguous().cpu().numpy().tobytes())
+    h.update(repr(sorted(atlas.cfg.__dict__.items())).encode())
+    return h.hexdigest()
+
+
 def warm_up(group=None, device=None):
     """Run each collective of merge_states once on a few bytes. The backend sets up its peer
     connections (NCCL: one channel per peer for the all-to-all) on first use; doing it here keeps
@@ -101,12 +160,9 @@ def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
         return atlas
     row_merge = row_merge or _row_merge_cuda
     # the shards must share edges, config and both seeds (atlas/core.py:632-634)
-    sig = torch.tensor([float(atlas.E.double().sum()), float(atlas.top_seed.double().nan_to_num(0, 0, 0).sum()),
-                        float(atlas.res_seed.double().sum()), float(zlib.crc32(repr(sorted(atlas.cfg.__dict__.items())).encode()))],
-                       dtype=torch.float64, device=atlas.top_k.device)
-    sigs = [torch.empty_like(sig) for _ in range(world)]
-    dist.all_gather(sigs, sig, group=group)
-    if not all(torch.equal(sigs[0], s) for s in sigs[1:]):
+    sigs = [None] * world
+    dist.all_gather_object(sigs, shard_signature(atlas), group=group)
+    if len(set(sigs)) != 1:
         raise ValueError("shards must share edges, config and seeds (derive them from the GLOBAL stream)")
     atlas.top_k, atlas.top_t, atlas.top_s = _exchange_rows(atlas.top_k, atlas.top_t, atlas.top_s, (-1, float("-inf")),
                                                            world, group, row_merge)
@@ -125,7 +181,7 @@ def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
         atlas.flush_gram()
         for l in range(atlas.gram64.shape[0]):
             g = atlas.gram64[l].to(dev)
-            atlas.gram64[l].copy_(_sum_in_rank_order(g, world, group).to(atlas.gram64.device))
+            atlas.gram64[l].copy_(_reduce_slices_in_rank_order(g, world, group).to(atlas.gram64.device))
         atlas.gram_rows = int(cnt[2])
     stats = [None] * world
     dist.all_gather_object(stats, dict(atlas.stats), group=group)

@@ -71,7 +71,7 @@ def sub_stats_into(XT, col0, n, E0, E1, levels, sum_, sq, bins, masks, n_pad):
 
 
 def sub_stats(X, E0, E1, levels, **_tile):
-    """Drop-in for stats_triton.sub_stats (stats_triton.py:163-203): X [n, D] (unit column stride);
+    """Drop-in for stats_triton.sub_stats (stats_triton.py:77-117): X [n, D] (unit column stride);
     returns (sum fp64 [D], sumsq fp64 [D], counts int32 [2, D, B], masks int8 [2, NL, D, n8])."""
     require_cuda(X, "X")
     assert X.stride(1) == 1
@@ -107,7 +107,7 @@ def gram_upper(XT, n: int, C):
 
 
 def gram_accumulate(X, C, **_tile):
-    """Drop-in for stats_triton.gram_accumulate (stats_triton.py:234-255): C [D, D] fp32 contiguous
+    """Drop-in for stats_triton.gram_accumulate (stats_triton.py:148-169): C [D, D] fp32 contiguous
     += X^T X on the upper block triangle (blocks of 128), in place; returns C."""
     require_cuda(X, "X")
     assert X.stride(1) == 1 and C.is_contiguous() and C.dtype == torch.float32

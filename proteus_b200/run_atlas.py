@@ -327,6 +327,17 @@ def main(argv=None):
 
     t2 = time.time()
     n_done = 0
+    # with several ranks every stop is collective (Lockstep): a rank that reaches its deadline or
+    # cap stops all ranks at the same step, and ranks whose shard is exhausted wait for the others,
+    # so no rank enters the combine's collectives while another still streams or has returned
+    from .dist import Lockstep
+    lock = Lockstep(device=dev if world > 1 else None)
+    STOP_CAP, STOP_DEADLINE = 1, 2
+
+    def finish_process_group():
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
     with torch.no_grad():
         src_iter = ds.batches(vocab, order, a.tokens_per_batch, plan=my_plan, start=start)
         if a.prefetch > 0:
@@ -334,66 +345,84 @@ def main(argv=None):
                                   for b in src_iter), a.prefetch)
         else:
             src_iter = ((b, None) for b in src_iter)
-        for bi, (b, ctx_host) in enumerate(src_iter, start=start):
-            tb = time.time()
-            ids, am = b.input_ids.to(dev, non_blocking=True), b.attention_mask.to(dev, non_blocking=True)
-            fwd_s = None
-            if a.pair_forward or (a.pair_every and bi % a.pair_every == 0):
-                atlas.enabled = False
-                sync(dev)
-                tf0 = time.time()
+        src_iter = iter(src_iter)
+        item = next(src_iter, None)
+        bi = start
+        while True:
+            want = 0
+            if item is not None:
+                b, ctx_host = item
+                tb = time.time()
+                ids, am = b.input_ids.to(dev, non_blocking=True), b.attention_mask.to(dev, non_blocking=True)
+                fwd_s = None
+                if a.pair_forward or (a.pair_every and bi % a.pair_every == 0):
+                    atlas.enabled = False
+                    sync(dev)
+                    tf0 = time.time()
+                    model(input_ids=ids, attention_mask=am)
+                    sync(dev)
+                    fwd_s = time.time() - tf0
+                    atlas.enabled = True
+                prof = None
+                if bi in a.profile_at:
+                    acts = [torch.profiler.ProfilerActivity.CPU]
+                    if torch.device(dev).type == "cuda":
+                        acts.append(torch.profiler.ProfilerActivity.CUDA)
+                    prof = torch.profiler.profile(activities=acts)
+                    prof.__enter__()
+                ta0 = time.time()
+                ctx = ctx_host.to(dev) if ctx_host is not None else atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann)
+                n_before = atlas.n_seen
+                atlas.begin_batch(ctx)
                 model(input_ids=ids, attention_mask=am)
+                redo = atlas.end_batch()
+                assert redo == []
+                gram_flushed = bi % a.gram_flush_every == a.gram_flush_every - 1
+                if gram_flushed:
+                    atlas.flush_gram()
                 sync(dev)
-                fwd_s = time.time() - tf0
-                atlas.enabled = True
-            prof = None
-            if bi in a.profile_at:
-                acts = [torch.profiler.ProfilerActivity.CPU]
-                if torch.device(dev).type == "cuda":
-                    acts.append(torch.profiler.ProfilerActivity.CUDA)
-                prof = torch.profiler.profile(activities=acts)
-                prof.__enter__()
-            ta0 = time.time()
-            ctx = ctx_host.to(dev) if ctx_host is not None else atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann)
-            n_before = atlas.n_seen
-            atlas.begin_batch(ctx)
-            model(input_ids=ids, attention_mask=am)
-            redo = atlas.end_batch()
-            assert redo == []
-            gram_flushed = bi % a.gram_flush_every == a.gram_flush_every - 1
-            if gram_flushed:
-                atlas.flush_gram()
-            sync(dev)
-            atlas_s = time.time() - ta0
-            if prof is not None:
-                prof.__exit__(None, None, None)
-                write_profile(prof, out / f"profile_batch_{bi}.txt", dev)
-                log(f"[atlas] profiled batch {bi} -> profile_batch_{bi}.txt")
-            rec = {"batch": bi, "n_seen_before": n_before, "n_valid": ctx.n_v, "rows": b.n_rows,
-                   "Lmax": int(b.input_ids.shape[1]), "seconds": time.time() - tb, "t_start": tb, "t_end": time.time(),
-                   "fwd_only_s": fwd_s, "atlas_pass_s": atlas_s,
-                   "overhead_vs_fwd": (atlas_s / fwd_s - 1) if fwd_s else None, "gram_flushed": gram_flushed,
-                   "flops": flops_per_batch(info, b.n_rows, b.input_ids.shape[1]), "redo_layers": []}
-            n_done += 1
-            last_ckpt_s = None
-            if (bi + 1) % a.ckpt_every == 0:
-                save_ckpt(bi + 1)
-            rec["ckpt_s"] = last_ckpt_s
-            logf.write(json.dumps(rec) + "\n")
-            logf.flush()
-            batch_s = max(batch_s, rec["seconds"]) if n_done > 2 else batch_s
-            if a.deadline and bi + 1 < len(my_plan) and time.time() > a.deadline - 2 * (batch_s + max(ckpt_s, 30.0)):
-                if (bi + 1) % a.ckpt_every:
-                    save_ckpt(bi + 1)
+                atlas_s = time.time() - ta0
+                if prof is not None:
+                    prof.__exit__(None, None, None)
+                    write_profile(prof, out / f"profile_batch_{bi}.txt", dev)
+                    log(f"[atlas] profiled batch {bi} -> profile_batch_{bi}.txt")
+                rec = {"batch": bi, "n_seen_before": n_before, "n_valid": ctx.n_v, "rows": b.n_rows,
+                       "Lmax": int(b.input_ids.shape[1]), "seconds": time.time() - tb, "t_start": tb,
+                       "t_end": time.time(), "fwd_only_s": fwd_s, "atlas_pass_s": atlas_s,
+                       "overhead_vs_fwd": (atlas_s / fwd_s - 1) if fwd_s else None, "gram_flushed": gram_flushed,
+                       "flops": flops_per_batch(info, b.n_rows, b.input_ids.shape[1]), "redo_layers": []}
+                n_done += 1
+                bi += 1
+                last_ckpt_s = None
+                if bi % a.ckpt_every == 0:
+                    save_ckpt(bi)
+                rec["ckpt_s"] = last_ckpt_s
+                logf.write(json.dumps(rec) + "\n")
+                logf.flush()
+                batch_s = max(batch_s, rec["seconds"]) if n_done > 2 else batch_s
+                item = next(src_iter, None)
+                if a.deadline and item is not None and \
+                        time.time() > a.deadline - 2 * (batch_s + max(ckpt_s, 30.0)):
+                    want = STOP_DEADLINE
+                elif a.stop_after and n_done >= a.stop_after:
+                    want = STOP_CAP
+            code, more = lock.agree(want, item is not None)
+            if code == STOP_DEADLINE:
+                if bi % a.ckpt_every:
+                    save_ckpt(bi)
                 writer.wait()
-                log(f"[atlas] deadline approaching: stopped cleanly at batch {bi + 1}; rerun with --resume")
+                log(f"[atlas] deadline approaching: stopped cleanly at batch {bi}; rerun with --resume")
+                finish_process_group()
                 return
-            if a.stop_after and n_done >= a.stop_after:
+            if code == STOP_CAP:
                 log(f"[atlas] stopping after {n_done} batches (simulated cap)")
                 writer.wait()
                 if rank == 0:
-                    (out / "run.json").write_text(json.dumps(summary(False, bi + 1), indent=1))
+                    (out / "run.json").write_text(json.dumps(summary(False, bi), indent=1))
+                finish_process_group()
                 return
+            if not more:
+                break
     writer.wait()
     logf.close()
     atlas.check_errors()

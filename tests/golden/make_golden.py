@@ -14,7 +14,7 @@ seeded inputs and stores every result field in compressed .npz files next to thi
   pilot.npz           pilot_edges / pilot_seeds with protein groups (reference.py:55-122)
   filter.npz          filter_candidates survivor sets + overflow count (filter_triton.py:65-86;
                       Triton interpreter on CPU)
-  sub_stats.npz       sub_stats counts, sums, masks (stats_triton.py:163-203; interpreter)
+  sub_stats.npz       sub_stats counts, sums, masks (stats_triton.py:77-117; interpreter)
   c1_esm8m.npz        BASELINE config 0: ESM-2 8M random-init fp32 CPU forward feeding the
                       reference Atlas (stats v1, merge loop), pilot edges + seeds from 64 sequences
 

@@ -76,8 +76,21 @@ def _worker(rank, world, port, mode, q):
         from proteus_b200.dist import merge_states, shard_plan, warm_up
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure before the combine")
+        if mode == "gram":  # the Gram's sliced all-to-all reduction against a plain rank-order sum
+            from proteus_b200.dist import _reduce_slices_in_rank_order
+            ts = [torch.from_numpy(np.random.default_rng(r).standard_normal((37, 53))) for r in range(world)]
+            want = ts[0].clone()
+            for t in ts[1:]:
+                want += t
+            got = _reduce_slices_in_rank_order(ts[rank].clone(), world, None)
+            q.put((rank, {"equal": bool(torch.equal(got, want))}))
+            torch.distributed.destroy_process_group()
+            return
         z = golden("merge_from")
         a = _shard(z, rank) if rank < 2 else _empty_shard(z)
+        if mode == "badsig" and rank == 1:
+            a.res_seed = a.res_seed.clone()
+            a.res_seed.view(-1)[7] += 1  # one seed differs: the shards were not seeded alike
         warm_up()
         merge_states(a, row_merge=cpu_row_merge, gram=False)
         want = {k[2:]: v for k, v in z.items() if k.startswith("m_")}
@@ -139,3 +152,78 @@ def test_failed_rank_ends_combine_with_error_not_hang():
     out = _run("fail")
     assert isinstance(out[1], str) and "injected failure" in out[1]
     assert isinstance(out[0], str), "rank 0 must see an error (timeout or peer loss), not a result"
+
+
+def _lockstep_worker(rank, world, port, plan_lens, stop_at, q):
+    """The run_atlas loop's control flow over a plan of plan_lens[rank] batches: rank r proposes a
+    deadline stop once it has streamed stop_at[r] batches (and has more left)."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import datetime
+        torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
+                                             timeout=datetime.timedelta(seconds=20))
+        from proteus_b200.dist import Lockstep
+        lock = Lockstep()
+        done, steps = 0, 0
+        while True:
+            want = 0
+            if done < plan_lens[rank]:
+                done += 1
+                if stop_at[rank] is not None and done >= stop_at[rank] and done < plan_lens[rank]:
+                    want = 2
+            code, more = lock.agree(want, done < plan_lens[rank])
+            steps += 1
+            if code or not more:
+                break
+        q.put((rank, (code, done, steps)))
+        torch.distributed.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"{type(e).__name__}: {e}\n{traceback.format_exc()[-400:]}"))
+
+
+def _run_lockstep(plan_lens, stop_at, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = len(plan_lens)
+    ps = [ctx.Process(target=_lockstep_worker, args=(r, world, port, plan_lens, stop_at, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r, v = q.get(timeout=timeout)
+        out[r] = v
+    for p in ps:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_lockstep_one_rank_at_deadline_stops_every_rank_at_the_same_step():
+    """plan[rank::world] gives the ranks plans of different lengths; rank 1 reaches its deadline
+    after 3 batches. Both ranks must stop at that step (rank 0 with 3 of its 7 batches done), not
+    rank 1 alone while rank 0 streams on towards the combine."""
+    out = _run_lockstep([7, 6], [None, 3])
+    assert out[0] == (2, 3, 3) and out[1] == (2, 3, 3), out
+
+
+def test_lockstep_uneven_shards_leave_the_loop_together():
+    """No stop: the rank with the shorter shard keeps agreeing until the longer one is done, so both
+    leave the loop at the same step and enter the combine together."""
+    out = _run_lockstep([7, 4], [None, None])
+    assert out[0] == (0, 7, 7) and out[1] == (0, 4, 7), out
+
+
+def test_gram_slices_reduce_in_rank_order():
+    """The Gram's combine (all-to-all of slices, rank-ordered sum, all-gather) equals the plain sum
+    of the ranks' matrices in rank order, bit for bit, with a size that does not divide by 3."""
+    out = _run("gram", world=3)
+    for r in range(3):
+        assert out[r] == {"equal": True}, out[r]
+
+
+def test_shards_with_different_seeds_are_refused():
+    out = _run("badsig")
+    for r in (0, 1):
+        assert isinstance(out[r], str) and "must share edges, config and seeds" in out[r], out[r]
