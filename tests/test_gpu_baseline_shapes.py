@@ -110,6 +110,9 @@ def test_c4_prefix_dual_sink_matches_reference_atlas():
     reference re-runs them densely (fed the same stored activations, so both arms see identical
     inputs), this build takes its in-hook dense path."""
     ref_core = _reference_core()
+    import psutil
+    if psutil.virtual_memory().available < 64 * 2**30:
+        pytest.skip("needs ~20 GB of host memory for the reference's host-side fp64 Gram (plus headroom)")
     from proteus_b200.core import Atlas, AtlasConfig
     from proteus_b200.data import SwissProt, shuffled_order, synthetic_dataset
     from proteus_b200.esm import attach, load, pilot
