@@ -122,7 +122,8 @@ def test_c4_prefix_dual_sink_matches_reference_atlas():
     data = synthetic_dataset(20000, seed=5, low_complexity=0.005)
     ds = SwissProt(data)
     plan = ds.plan(shuffled_order(len(ds), 5), tpb, seed=5)
-    lowc = [i for i in range(len(ds)) if bool(data["low_complexity"][i])]
+    streamed = {i for grp in plan[:8] for i in grp}  # token ids must stay unique across the stream
+    lowc = [i for i in range(len(ds)) if bool(data["low_complexity"][i]) and i not in streamed]
     lc_batch = []
     for i in lowc:  # one batch of low-complexity sequences only
         if (len(lc_batch) + 1) * (min(int(ds.len[i]), ds.max_res) + 2) > tpb or len(lc_batch) >= 40:
