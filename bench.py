@@ -686,8 +686,7 @@ def main():
     attach(model, atlas.observe)
     host = []
     for grp in mine:
-        b = ds._make(grp, {c: vocab.get(c, vocab["<unk>"]) for c in "ACDEFGHIKLMNPQRSTVWYXBUZO"},
-                     vocab["<cls>"], vocab["<eos>"], vocab["<pad>"])
+        b = ds.make_batch(grp, vocab)
         host.append((b, atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann, device="cpu")))
     W, K, P = args.warmup, args.steps, args.preroll
     # the e2e pass replays the timed batches from the same atlas state (restored snapshot), so both

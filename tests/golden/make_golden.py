@@ -15,6 +15,8 @@ seeded inputs and stores every result field in compressed .npz files next to thi
   filter.npz          filter_candidates survivor sets + overflow count (filter_triton.py:65-86;
                       Triton interpreter on CPU)
   sub_stats.npz       sub_stats counts, sums, masks (stats_triton.py:77-117; interpreter)
+  data_plan.npz       SwissProt batch plan, pilot plan, coverage and batch tensors on a dataset
+                      with truncation, odd letters and deep annotation overlaps (atlas/data.py)
   c1_esm8m.npz        BASELINE config 0: ESM-2 8M random-init fp32 CPU forward feeding the
                       reference Atlas (stats v1, merge loop), pilot edges + seeds from 64 sequences
 
@@ -295,6 +297,78 @@ def gen_c1():
     print(f"c1: {time.time() - t0:.1f}s, n_seen {res['n_seen']}, stats {res['stats']}", flush=True)
 
 
+DATA_CASE = dict(n_seq=3000, seed=4, tokens_per_batch=8192, window=1000, pilot_tokens=20000, batches=(0, 3, -1))
+
+
+DATA_X_GROUP = [7, 11, 2, 40]
+
+
+def data_case() -> dict:
+    """A dataset in the reference's on-disk format that exercises every rule of the batch plan and
+    of the annotation fill: lengths from 5 to 1500 (truncation at 1022, equal lengths whose order a
+    stable sort must keep), letters outside the standard 20 (X B U Z O and a lowercase one), and
+    annotation intervals that run past the truncated end, are empty after truncation, or pile up
+    more than max_ann deep."""
+    import torch
+    rng = np.random.default_rng(DATA_CASE["seed"])
+    n = DATA_CASE["n_seq"]
+    lens = np.clip(np.round(rng.lognormal(np.log(250), 0.8, n)), 5, 1500).astype(np.int32)
+    lens[::97] = 300  # repeated lengths
+    lens[40] = 1500  # truncated; one interval lies entirely past its truncated end
+    letters = np.frombuffer(b"ACDEFGHIKLMNPQRSTVWYXBUZOa", np.uint8)
+    p = np.r_[np.full(20, 0.049), np.full(6, 0.02 / 6)]
+    seqs = [letters[rng.choice(26, int(m), p=p / p.sum())].tobytes().decode() for m in lens]
+    iv = []
+    for i in rng.choice(n, 1500, replace=False):
+        m = int(lens[i])
+        for _ in range(int(rng.integers(1, 5))):
+            a0 = int(rng.integers(0, m))
+            iv.append((i, a0, int(min(m + 5, a0 + rng.integers(1, 80))), int(rng.integers(21, 60))))
+    for i in (7, 11):  # 12 intervals over one region: more than max_ann - 1 = 7 extra columns
+        for k in range(12):
+            iv.append((i, 1, 4 + k, 30 + k))
+    iv.append((40, 1100, 1200, 50))  # entirely past the truncated end
+    iv = np.array(iv, np.int32)[rng.permutation(len(iv))]
+    return {"acc": [f"T{i:05d}" for i in range(n)], "seq": seqs, "len": torch.from_numpy(lens),
+            "iv": torch.from_numpy(iv), "vocab": [f"a{k}" for k in range(60)]}
+
+
+def gen_data():
+    """The reference's SwissProt (atlas/data.py) on data_case(): plans, pilot plan, coverage, and
+    the tensors of a few batches."""
+    import io
+
+    import torch
+    from atlas.data import SwissProt, shuffled_order
+    from tests.c1 import ESM_TOKENS
+    c = DATA_CASE
+    buf = io.BytesIO()
+    torch.save(data_case(), buf)
+    buf.seek(0)
+    ds = SwissProt(buf)
+    vocab = {t: i for i, t in enumerate(ESM_TOKENS)}
+    order = shuffled_order(len(ds), c["seed"])
+    out = {"order": _np(order)}
+    plans = {"shuffled": ds.plan(order, c["tokens_per_batch"], c["window"], c["seed"]),
+             "sorted": ds.plan(order, c["tokens_per_batch"], c["window"], c["seed"], shuffle_batches=False)}
+    plans["pilot"] = ds.pilot_plan(plans["shuffled"], c["pilot_tokens"], c["tokens_per_batch"], c["seed"])
+    for name, pl in plans.items():
+        out[f"plan_{name}_flat"] = np.array([i for g in pl for i in g], np.int64)
+        out[f"plan_{name}_sizes"] = np.array([len(g) for g in pl], np.int64)
+    cov = ds.coverage(order[:500])
+    out.update({f"cov_{k}": np.array(v) for k, v in cov.items()})
+    aa = {ch: vocab.get(ch, vocab["<unk>"]) for ch in set("ACDEFGHIKLMNPQRSTVWY") | set("XBUZO")}
+    groups = {bi: plans["shuffled"][bi] for bi in c["batches"]}
+    groups["x"] = DATA_X_GROUP  # the sequences with the deep interval piles and the longest one
+    for bi, grp in groups.items():
+        b = ds._make(grp, aa, vocab["<cls>"], vocab["<eos>"], vocab["<pad>"])
+        for k in ("input_ids", "attention_mask", "valid_rows", "tok", "ann", "seq_idx"):
+            out[f"b{bi}_{k}"] = _np(getattr(b, k))
+        out[f"b{bi}_n_rows"] = np.int64(b.n_rows)
+    out["ann_dropped"] = np.int64(ds.ann_dropped)
+    np.savez_compressed(HERE / "data_plan.npz", **out)
+
+
 C1_DIGEST_FIELDS = ("top_val", "top_tok", "res_tok", "res_val", "res_key", "sub_bin", "enr", "ann_tot",
                     "res_seed_limited", "res_seed_key")
 
@@ -329,7 +403,8 @@ def main():
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     jobs = {"streams": gen_streams, "keys": gen_keys, "grouped_merge": gen_grouped_merge,
-            "merge_from": gen_merge_from, "pilot": gen_pilot, "kernels": gen_kernels, "c1": gen_c1}
+            "merge_from": gen_merge_from, "pilot": gen_pilot, "kernels": gen_kernels, "c1": gen_c1,
+            "data": gen_data}
     for name, fn in jobs.items():
         if a.only is None or name in a.only:
             t0 = time.time()

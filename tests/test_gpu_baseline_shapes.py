@@ -135,8 +135,7 @@ def test_c4_prefix_dual_sink_matches_reference_atlas():
     model, vocab, info = load("650M", dtype=torch.bfloat16, device=dev, seed=5)
     voc = vocab.get_vocab()
     L, D = info["n_layers"], info["d_ff"]
-    aa = {c: voc.get(c, voc["<unk>"]) for c in "ACDEFGHIKLMNPQRSTVWYXBUZO"}
-    mk = lambda grp: ds._make(grp, aa, voc["<cls>"], voc["<eos>"], voc["<pad>"])  # noqa: E731
+    mk = lambda grp: ds.make_batch(grp, voc)  # noqa: E731
     pplan = ds.pilot_plan(plan, 65536, tpb, seed=5)
     Hp, _ = pilot(model, (mk(g) for g in pplan), dev, 1 << 62, store_device=dev)
     prot = (pilot.last_tok // 1024).to(dev)
