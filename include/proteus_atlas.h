@@ -221,6 +221,42 @@ int atlas_grouped_merge_static(int64_t* state_sc, int64_t* state_tok, float* sta
 int atlas_merge_rows(int64_t* sc, int64_t* tok, float* val, const int64_t* other_sc, const int64_t* other_tok,
                      const float* other_val, int64_t G, int64_t K, void* stream);
 
+/* ------------------------------------------------------------------------------------------------
+ * Pilot pass — replaces the sorts and top-k selections of pilot_edges / pilot_seeds
+ * (atlas/reference.py:55-122) with exact order statistics and integer counts on the device.
+ *
+ * atlas_column_select: out[d, t] = the value at ascending rank ranks_host[t] (0-based, < n) of the
+ *   n elements XT[d, 0..n) (transposed activations, leading dimension ldx % 8 == 0, 16-byte aligned
+ *   base), for every d < D; 1 <= R <= 32 ranks; -0.0 ranks below +0.0 (the order of a radix sort of
+ *   the float bits). Values are returned as fp32 (exact for every dtype).
+ * atlas_pilot_edges: sel [D, 2B] holds, per column, the values at ranks r_b = round(q_b (n-1)) and
+ *   at n-1-r_b; writes E [2, D, B] with E[0, d, b] = sel[d, b], E[1, d, b] = -sel[d, B + b], each
+ *   then raised to nextafter(E[p, d, b-1], +inf) where not above it (strictly increasing edges).
+ * atlas_pilot_counts: for the rows visited in the order `order` (int32 row indices, NULL = 0..n-1),
+ *   per pole p (s = +h, -h), column d and bin b (bin = #{b : s >= E[p, d, b]} - 1):
+ *     cnt[(p*D + d)*B + b]   += #{rows in the bin}
+ *     sumsq[(p*D + d)*B + b] += sum over runs of (#{rows of the run in the bin})^2
+ *   where a run ends at every visited position i with run_last[i] != 0 (run_last NULL: no runs,
+ *   sumsq untouched). chunk_start (device int64 [n_chunks + 1], 0 = first, n = last) splits the
+ *   visiting order into pieces of whole runs worked on in parallel. cnt, sumsq: int64 [2, D, B].
+ * atlas_pilot_seeds: per pole and column, top_seed[p*D + d] = nextafter(v, -inf) with v = sel2[d, 0]
+ *   (p = 0) or -sel2[d, 1] (p = 1), sel2 [D, 2] the values at ascending ranks n-kk and kk-1
+ *   (kk = min(2K, n)); per bin the key ceiling
+ *     grouped:   n_eff = cnt^2 / max(sumsq, 1); m_lo = (cnt / n) * max(1 - z / sqrt(max(n_eff, 1e-9)), 0)
+ *     otherwise: m_lo = max(cnt - z * sqrt(cnt), 0) / n
+ *     res_seed_key = floor(min(m_lo > 0 ? c*Kr*2^32 / (n_total * m_lo) : 2^32, 2^32))
+ *   in fp64 with the reference's operation order (each operation correctly rounded).
+ */
+int atlas_column_select(const void* XT, int dtype, int64_t ldx, int64_t n, int64_t D, const int64_t* ranks_host,
+                        int64_t R, float* out, void* stream);
+int atlas_pilot_edges(const float* sel, int64_t D, int64_t B, float* E, void* stream);
+int atlas_pilot_counts(const void* H, int dtype, int64_t ld, int64_t n, int64_t D, const int32_t* order,
+                       const uint8_t* run_last, const int64_t* chunk_start, int64_t n_chunks, const float* E,
+                       int64_t B, int64_t* cnt, int64_t* sumsq, void* stream);
+int atlas_pilot_seeds(const int64_t* cnt, const int64_t* sumsq, const float* sel2, int64_t D, int64_t B, int64_t n,
+                      int64_t Kr, int64_t n_total, double c, double z, int grouped, float* top_seed,
+                      int64_t* res_seed_key, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -618,9 +618,16 @@ def pilot_edges(Hs, probs=(0.5, 0.9, 0.99, 0.999, 0.9999)) -> np.ndarray:
     return E
 
 
-def pilot_seeds(Hs, E, K, Kr, n_total, c=4.0, z=2.0):
-    """Seeds without protein groups (reference.py:78-122, groups=None branch)."""
+def pilot_seeds(Hs, E, K, Kr, n_total, c=4.0, z=2.0, groups=None):
+    """Seeds (reference.py:78-122): top seed = nextafter(2K-th largest pilot s, -inf); reservoir key
+    ceilings from a z-sigma lower bound of the pilot bin mass; with protein `groups` [n] the bound
+    uses the effective count n_eff = (sum_g c_g)^2 / sum_g c_g^2 over the groups' bin counts."""
     tops, keys = [], []
+    if groups is not None:
+        g = np.asarray(groups, np.int64).reshape(-1)
+        order = np.argsort(g, kind="stable")
+        gs = g[order]
+        run_starts = np.nonzero(np.r_[True, gs[1:] != gs[:-1]])[0]
     for li, H in enumerate(Hs):
         n, D = H.shape
         kk = min(2 * K, n)
@@ -632,7 +639,12 @@ def pilot_seeds(Hs, E, K, Kr, n_total, c=4.0, z=2.0):
             ge = s[..., None] >= E[li, p][None]
             in_bin = ge & ~np.concatenate((ge[..., 1:], np.zeros_like(ge[..., :1])), -1)
             cnt = in_bin.sum(0).astype(np.float64)
-            m_lo = np.maximum(cnt - z * np.sqrt(cnt), 0) / n
+            if groups is None:
+                m_lo = np.maximum(cnt - z * np.sqrt(cnt), 0) / n
+            else:
+                per = np.add.reduceat(in_bin[order].astype(np.int32), run_starts, axis=0).astype(np.int64)
+                n_eff = cnt * cnt / np.maximum((per * per).sum(0).astype(np.float64), 1)  # per: [groups, D, B]
+                m_lo = (cnt / n) * np.maximum(1 - z / np.sqrt(np.maximum(n_eff, 1e-9)), 0)
             with np.errstate(divide="ignore"):
                 theta = np.where(m_lo > 0, c * Kr * 2.0**32 / (n_total * m_lo), 2.0**32)
             kp.append(np.floor(np.minimum(theta, 2.0**32)).astype(np.int64))

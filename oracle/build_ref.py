@@ -6,8 +6,9 @@ use this module; the product path never does.
 The reference (haelyons/proteus) is Python. The Python analogue of compiling a C reference from its
 sources into a binary is byte-compiling its modules: `build()` compiles the hot-path modules of the
 reference's `atlas/` package, where they lie in the reference checkout, into sourceless bytecode
-files under oracle/_ref/atlas/ (`<module>.pyc` beside each other, which the interpreter imports
-without a source file). No source file is copied. oracle/_ref/ is git-ignored, so nothing of it
+files oracle/_ref/atlas/<module>.bytecode (the .pyc format under another suffix, since snapshots of
+the repository leave .pyc files behind), which `load_reference_atlas` imports through a path finder
+of its own. No source file is copied. oracle/_ref/ is git-ignored, so nothing of it
 enters the history, but it is not excluded from the GPU-box snapshot, so the reference's own CPU
 implementation can run there: as the timed reference arm of bench.py and as the second sink of the
 dual-sink parity tests. The bytecode is tied to the interpreter version that built it (the GPU box
@@ -22,6 +23,9 @@ from __future__ import annotations
 
 import argparse
 import importlib
+import importlib.abc
+import importlib.machinery
+import importlib.util
 import json
 import os
 import py_compile
@@ -53,6 +57,9 @@ def reference_root(ref: str | os.PathLike | None = None) -> Path | None:
     return None
 
 
+SUFFIX = ".bytecode"
+
+
 def build(ref: str | os.PathLike | None = None, out: Path = OUT) -> Path | None:
     """Byte-compile the reference's hot-path modules into out/atlas/. Returns out, or None when the
     reference checkout is absent (then an earlier build, if any, is left as it is)."""
@@ -65,19 +72,41 @@ def build(ref: str | os.PathLike | None = None, out: Path = OUT) -> Path | None:
         src = root / "atlas" / f"{m}.py"
         if not src.exists():
             continue
-        py_compile.compile(str(src), cfile=str(pkg / f"{m}.pyc"), dfile=f"atlas/{m}.py", doraise=True,
+        py_compile.compile(str(src), cfile=str(pkg / f"{m}{SUFFIX}"), dfile=f"atlas/{m}.py", doraise=True,
                            invalidation_mode=py_compile.PycInvalidationMode.UNCHECKED_HASH)
     (out / "BUILT_FROM").write_text(f"python {sys.version.split()[0]}\nmodules {' '.join(MODULES)}\n")
     return out
 
 
 def available(out: Path = OUT) -> bool:
-    return (out / "atlas" / "core.pyc").exists()
+    return (out / "atlas" / f"core{SUFFIX}").exists()
+
+
+class _CompiledReferenceFinder(importlib.abc.MetaPathFinder):
+    """Finds `atlas` and `atlas.<module>` among the compiled files of oracle/_ref."""
+
+    def __init__(self, out: Path):
+        self.pkg = out / "atlas"
+
+    def find_spec(self, fullname, path=None, target=None):
+        if fullname != "atlas" and not fullname.startswith("atlas."):
+            return None
+        leaf = "__init__" if fullname == "atlas" else fullname.split(".", 1)[1]
+        f = self.pkg / f"{leaf}{SUFFIX}"
+        if "." in leaf or not f.exists():
+            return None
+        loader = importlib.machinery.SourcelessFileLoader(fullname, str(f))
+        return importlib.util.spec_from_file_location(
+            fullname, str(f), loader=loader, submodule_search_locations=[str(self.pkg)] if leaf == "__init__" else None)
+
+
+_FINDER: _CompiledReferenceFinder | None = None
 
 
 def load_reference_atlas(out: Path = OUT):
     """Import the compiled reference package and return its `atlas.core` module. Raises
     ReferenceUnavailable when oracle/_ref has not been built or was built by another interpreter."""
+    global _FINDER
     if not available(out):
         raise ReferenceUnavailable("oracle/_ref has not been built (python -m oracle.build_ref, needs the reference)")
     mod = sys.modules.get("atlas.core")
@@ -85,25 +114,19 @@ def load_reference_atlas(out: Path = OUT):
         return mod
     if "atlas" in sys.modules and not str(getattr(sys.modules["atlas"], "__file__", "")).startswith(str(out)):
         raise ReferenceUnavailable("another package named 'atlas' is already imported")
-    sys.path.insert(0, str(out))
+    if _FINDER is None:
+        _FINDER = _CompiledReferenceFinder(out)
+        sys.meta_path.insert(0, _FINDER)
     try:
         return importlib.import_module("atlas.core")
     except ImportError as e:  # bad magic number (other interpreter) and the like
         raise ReferenceUnavailable(f"compiled reference cannot be imported: {e}") from e
-    finally:
-        if sys.path and sys.path[0] == str(out):
-            sys.path.pop(0)
 
 
 def load_reference_module(name: str, out: Path = OUT):
     """Another module of the compiled reference package (e.g. "reference", "data")."""
     load_reference_atlas(out)
-    sys.path.insert(0, str(out))
-    try:
-        return importlib.import_module(f"atlas.{name}")
-    finally:
-        if sys.path and sys.path[0] == str(out):
-            sys.path.pop(0)
+    return importlib.import_module(f"atlas.{name}")
 
 
 def main():

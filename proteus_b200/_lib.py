@@ -27,8 +27,8 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "proteus_atlas.h"
 def parse_header(path: Path = HEADER) -> dict:
     """name -> (restype, argtypes) for every function declared in include/proteus_atlas.h.
 
-    Pointers map to c_void_p, int64_t to c_int64, int to c_int, so the binding cannot drift from
-    the header."""
+    Pointers map to c_void_p, int64_t to c_int64, int to c_int, double to c_double, so the binding
+    cannot drift from the header."""
     text = re.sub(r"/\*.*?\*/", " ", path.read_text(), flags=re.S)
     sigs = {}
     for m in re.finditer(r"(const\s+char\s*\*|int64_t|int)\s+(atlas_\w+)\s*\(([^)]*)\)\s*;", text):
@@ -45,6 +45,8 @@ def parse_header(path: Path = HEADER) -> dict:
                 args.append(_L)
             elif prm.startswith("int "):
                 args.append(_I)
+            elif prm.startswith("double "):
+                args.append(C.c_double)
             else:
                 raise ValueError(f"unparsed parameter {prm!r} of {name}")
         sigs[name] = (rtype, args)

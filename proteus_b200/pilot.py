@@ -1,78 +1,127 @@
-"""Pilot-pass math: bin edges and exact-preserving seeds — drop-in for haelyons/proteus
-atlas/reference.py:pilot_edges / pilot_seeds (reference.py:55-122).
+"""Pilot pass on the device: bin edges and exact-preserving seeds — drop-in for haelyons/proteus
+atlas/reference.py:pilot_edges / pilot_seeds (reference.py:55-122), same arguments and results.
 
-Runs once per run on the device holding the pilot activations (PyTorch ops; not on the per-batch
-hot path). One column-chunk sort serves both poles: the pole-1 order statistics are the negated
-pole-0 ones read from the other end.
+The reference sorts every column (torch.sort) for the edges and takes a top-k per column for the top
+seed. Both only need a few order statistics per column, so here they are exact radix selections on
+the device (atlas_column_select over the transposed pilot activations), and the bin masses and
+per-protein counts behind the reservoir seeds are integer counts (atlas_pilot_counts), finished by
+the reference's fp64 arithmetic in atlas_pilot_seeds. Activations must be on a CUDA device (bf16,
+fp16 or fp32); there is no CPU path.
+
+  edges  E[l, 0, d, b] = value at rank round(q_b (n-1)) of column d;  E[l, 1, d, b] = the same for
+         s = -h; forced strictly increasing along b with nextafter(., +inf)
+  seeds  top_seed[l, p, d] = nextafter(2K-th largest s, -inf); res_seed_key[l, p, d, b] = key
+         ceiling with c*Kr expected keys below it over the stream, from a z-sigma lower bound of the
+         bin's pilot mass (with protein groups: effective count n_eff = (sum c_i)^2 / sum c_i^2)
 """
 from __future__ import annotations
 
 import torch
 
+from ._lib import AtlasKernelError, call, dtype_code, ptr, stream_ptr
 
-def _quantile_rows(n: int, probs) -> list[int]:
+ROWS_PER_CHUNK = 4096  # pilot rows per CTA column-strip in the count kernel
+
+
+def _device_input(H: torch.Tensor) -> torch.Tensor:
+    if not H.is_cuda:
+        raise AtlasKernelError("pilot activations must be on a CUDA device: the pilot runs on the sm_100a kernels")
+    if H.dim() != 2 or H.shape[0] < 1:
+        raise ValueError(f"pilot activations must be [n >= 1, D], got {tuple(H.shape)}")
+    return H if H.stride(1) == 1 else H.contiguous()
+
+
+def _transposed(H: torch.Tensor) -> torch.Tensor:
+    """XT [D, ldx] (ldx = n rounded up to 8) holding H transposed (atlas_gather_transpose)."""
+    n, D = H.shape
+    ldx = -(-n // 8) * 8
+    XT = torch.empty(D, ldx, dtype=H.dtype, device=H.device)
+    rows = torch.arange(n, dtype=torch.int32, device=H.device)
+    call("atlas_gather_transpose", ptr(H), dtype_code(H.dtype), n, D, H.stride(0), ptr(rows), n, ptr(XT), ldx, 0,
+         stream_ptr(H.device))
+    return XT
+
+
+def column_values_at_ranks(H: torch.Tensor, ranks: list[int]) -> torch.Tensor:
+    """[D, len(ranks)] fp32: per column of H [n, D], the values at the given ascending ranks."""
+    import ctypes
+    H = _device_input(H)
+    n, D = H.shape
+    XT = _transposed(H)
+    out = torch.empty(D, len(ranks), dtype=torch.float32, device=H.device)
+    rk = (ctypes.c_int64 * len(ranks))(*ranks)
+    call("atlas_column_select", ptr(XT), dtype_code(H.dtype), XT.stride(0), n, D, ctypes.cast(rk, ctypes.c_void_p),
+         len(ranks), ptr(out), stream_ptr(H.device))
+    return out
+
+
+def _quantile_ranks(n: int, probs) -> list[int]:
     return [min(n - 1, int(round(q * (n - 1)))) for q in probs]
 
 
 def pilot_edges(Hs: list, probs=(0.5, 0.9, 0.99, 0.999, 0.9999), chunk: int = 512) -> torch.Tensor:
-    """E[l, p, d, b] = probs[b]-quantile (row round(q*(n-1)) of the sorted column) of s = +h / -h,
-    forced strictly increasing along b. Returns [L, 2, D, B] fp32 on the input's device."""
+    """E [L, 2, D, B] fp32 on the activations' device (`chunk`, the reference's column chunk of its
+    sort, is accepted and unused)."""
     out = []
     for H in Hs:
+        H = _device_input(H)
         n, D = H.shape
-        idx = torch.tensor(_quantile_rows(n, probs), device=H.device)
-        ridx = (n - 1) - idx
-        p0, p1 = [], []
-        for c0 in range(0, D, chunk):
-            s, _ = torch.sort(H[:, c0:c0 + chunk].float(), dim=0)
-            p0.append(s.index_select(0, idx).T)
-            p1.append((-s.index_select(0, ridx)).T)  # sort(-h)[i] == -sort(h)[n-1-i]
-            del s
-        out.append(torch.stack([torch.cat(p0), torch.cat(p1)]))
-    E = torch.stack(out)
-    for b in range(1, E.shape[-1]):
-        E[..., b] = torch.maximum(E[..., b], torch.nextafter(E[..., b - 1], torch.full_like(E[..., b - 1], float("inf"))))
-    return E
+        r = _quantile_ranks(n, probs)
+        B = len(r)
+        sel = column_values_at_ranks(H, r + [(n - 1) - x for x in r])
+        E = torch.empty(2, D, B, dtype=torch.float32, device=H.device)
+        call("atlas_pilot_edges", ptr(sel), D, B, ptr(E), stream_ptr(H.device))
+        out.append(E)
+    return torch.stack(out)
+
+
+def _visiting_order(groups: torch.Tensor | None, n: int, dev):
+    """(order int32 | None, run_last uint8 | None, chunk_start int64): rows grouped by protein
+    (stable), the end of each protein's run, and chunk starts at run starts."""
+    if groups is None:
+        starts = torch.arange(0, n, ROWS_PER_CHUNK, dtype=torch.int64, device=dev)
+        return None, None, torch.cat([starts, torch.tensor([n], dtype=torch.int64, device=dev)])
+    g = groups.reshape(-1).to(dev, torch.int64)
+    if g.numel() != n:
+        raise ValueError(f"groups has {g.numel()} entries for {n} pilot rows")
+    order = torch.argsort(g, stable=True)
+    gs = g[order]
+    change = torch.ones(n, dtype=torch.bool, device=dev)
+    change[1:] = gs[1:] != gs[:-1]                       # first row of each run
+    run_last = torch.ones(n, dtype=torch.uint8, device=dev)
+    run_last[:-1] = change[1:].to(torch.uint8)           # last row of each run
+    run_starts = torch.nonzero(change).squeeze(1)
+    n_chunks = max(1, min(65535, -(-n // ROWS_PER_CHUNK)))
+    want = torch.arange(n_chunks, dtype=torch.int64, device=dev) * n // n_chunks
+    pos = torch.searchsorted(run_starts, want).clamp(max=run_starts.numel() - 1)
+    starts = torch.unique(run_starts[pos])
+    return order.to(torch.int32), run_last, torch.cat([starts, torch.tensor([n], dtype=torch.int64, device=dev)])
 
 
 def pilot_seeds(Hs: list, E: torch.Tensor, K: int, Kr: int, n_total: int, c: float = 4.0, z: float = 2.0,
                 chunk: int = 512, groups: torch.Tensor | None = None):
-    """Seeds from pilot activations of tokens that are also streamed (reference.py:78-122):
-    top_seed [L,2,D] = nextafter(2K-th largest pilot s, -inf); res_seed_key [L,2,D,B] = floor of
-    c*Kr*2^32 / (n_total * m_lo) clamped to 2^32, m_lo a z-sigma lower bound of the pilot bin mass
-    (with protein groups: effective count n_eff = (sum c_i)^2 / sum c_i^2). Returns CPU tensors."""
-    if groups is not None:
-        _, gidx = torch.unique(groups, return_inverse=True)
-        n_g = int(gidx.max()) + 1
-        chunk = min(chunk, 128)
+    """(top_seed [L, 2, D] fp32, res_seed_key [L, 2, D, B] int64), CPU tensors, from pilot activations
+    of tokens that are also streamed; `groups` [n] gives each pilot row's protein (`chunk` is
+    accepted and unused)."""
     tops, keys = [], []
     for li, H in enumerate(Hs):
+        H = _device_input(H)
         n, D = H.shape
+        dev = H.device
+        El = E[li].to(dev, torch.float32).contiguous()
+        B = El.shape[-1]
         kk = min(2 * K, n)
-        tp, kp = [], []
-        for p, sgn in ((0, 1.0), (1, -1.0)):
-            t_cols, k_cols = [], []
-            Ep = E[li, p].to(H.device)
-            for c0 in range(0, D, chunk):
-                s = H[:, c0:c0 + chunk].float() * sgn
-                t = torch.topk(s, kk, dim=0).values[kk - 1]
-                t_cols.append(torch.nextafter(t, torch.full_like(t, float("-inf"))))
-                ge = s.unsqueeze(-1) >= Ep[c0:c0 + chunk]
-                in_bin = ge & ~torch.cat((ge[..., 1:], torch.zeros_like(ge[..., :1])), -1)
-                cnt = in_bin.sum(0).double()
-                if groups is None:
-                    m_lo = (cnt - z * cnt.sqrt()).clamp(min=0) / n
-                else:
-                    per = torch.zeros((n_g,) + tuple(cnt.shape), dtype=torch.float32, device=s.device)
-                    per.index_add_(0, gidx.to(s.device), in_bin.float())
-                    n_eff = cnt ** 2 / (per.double() ** 2).sum(0).clamp(min=1)
-                    m_lo = (cnt / n) * (1 - z / n_eff.clamp(min=1e-9).sqrt()).clamp(min=0)
-                    del per
-                theta = torch.where(m_lo > 0, c * Kr * 2.0**32 / (n_total * m_lo), torch.full_like(m_lo, 2.0**32))
-                k_cols.append(theta.clamp(max=2.0**32).floor().to(torch.int64))
-                del s, ge, in_bin
-            tp.append(torch.cat(t_cols))
-            kp.append(torch.cat(k_cols))
-        tops.append(torch.stack(tp))
-        keys.append(torch.stack(kp))
+        sel2 = column_values_at_ranks(H, [n - kk, kk - 1])
+        order, run_last, cstart = _visiting_order(groups, n, dev)
+        cnt = torch.zeros(2, D, B, dtype=torch.int64, device=dev)
+        sq = torch.zeros(2, D, B, dtype=torch.int64, device=dev)
+        st = stream_ptr(dev)
+        call("atlas_pilot_counts", ptr(H), dtype_code(H.dtype), H.stride(0), n, D, ptr(order), ptr(run_last),
+             ptr(cstart), cstart.numel() - 1, ptr(El), B, ptr(cnt), ptr(sq), st)
+        top = torch.empty(2, D, dtype=torch.float32, device=dev)
+        key = torch.empty(2, D, B, dtype=torch.int64, device=dev)
+        call("atlas_pilot_seeds", ptr(cnt), ptr(sq), ptr(sel2), D, B, n, Kr, int(n_total), float(c), float(z),
+             int(groups is not None), ptr(top), ptr(key), st)
+        tops.append(top)
+        keys.append(key)
     return torch.stack(tops).cpu(), torch.stack(keys).cpu()

@@ -189,24 +189,65 @@ def _dataset(spec: str):
     return SwissProt(spec)
 
 
-def _prefetch(it, n):
-    q, end = queue.Queue(maxsize=n), object()
+class Prefetch:
+    """Items of `it` produced `n` ahead on a background thread (the batch and its host-side context,
+    as the reference's prefetch thread builds them). `close()` stops the producer and joins it: the
+    producer checks the stop flag between items, and close() drains the queue so a producer blocked
+    on a full queue wakes up. Every exit path of the stream loop closes it, so no producer is still
+    inside a torch op when the interpreter shuts down."""
 
-    def work():
+    _END = object()
+
+    def __init__(self, it, n):
+        self._q = queue.Queue(maxsize=max(1, n))
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._work, args=(it,), name="prefetch", daemon=True)
+        self._t.start()
+
+    def _work(self, it):
         try:
             for x in it:
-                q.put(x)
-        except BaseException as e:  # noqa: BLE001
-            q.put(e)
-        q.put(end)
-    threading.Thread(target=work, daemon=True).start()
-    while True:
-        x = q.get()
-        if x is end:
+                while not self._stop.is_set():
+                    try:
+                        self._q.put(x, timeout=0.1)
+                        break
+                    except queue.Full:
+                        continue
+                if self._stop.is_set():
+                    return
+        except BaseException as e:  # noqa: BLE001  re-raised on the consumer's thread
+            self._put_final(e)
             return
+        self._put_final(self._END)
+
+    def _put_final(self, x):
+        while not self._stop.is_set():
+            try:
+                self._q.put(x, timeout=0.1)
+                return
+            except queue.Full:
+                continue
+
+    def __iter__(self):
+        return self
+
+    def __next__(self):
+        x = self._q.get()
+        if x is self._END:
+            raise StopIteration
         if isinstance(x, BaseException):
             raise x
-        yield x
+        return x
+
+    def close(self):
+        self._stop.set()
+        while self._t.is_alive():
+            try:
+                while True:
+                    self._q.get_nowait()
+            except queue.Empty:
+                pass
+            self._t.join(timeout=0.1)
 
 
 def main(argv=None):
@@ -338,14 +379,9 @@ def main(argv=None):
         if world > 1:
             torch.distributed.destroy_process_group()
 
-    with torch.no_grad():
-        src_iter = ds.batches(vocab, order, a.tokens_per_batch, plan=my_plan, start=start)
-        if a.prefetch > 0:
-            src_iter = _prefetch(((b, atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann, device="cpu"))
-                                  for b in src_iter), a.prefetch)
-        else:
-            src_iter = ((b, None) for b in src_iter)
-        src_iter = iter(src_iter)
+    def _stream(src_iter):
+        """The batch loop; returns the agreed stop code (None after the whole plan)."""
+        nonlocal n_done, batch_s, last_ckpt_s
         item = next(src_iter, None)
         bi = start
         while True:
@@ -412,17 +448,33 @@ def main(argv=None):
                     save_ckpt(bi)
                 writer.wait()
                 log(f"[atlas] deadline approaching: stopped cleanly at batch {bi}; rerun with --resume")
-                finish_process_group()
-                return
+                return code
             if code == STOP_CAP:
                 log(f"[atlas] stopping after {n_done} batches (simulated cap)")
                 writer.wait()
                 if rank == 0:
                     (out / "run.json").write_text(json.dumps(summary(False, bi), indent=1))
-                finish_process_group()
-                return
+                return code
             if not more:
-                break
+                return None
+
+    prefetch = None
+    with torch.no_grad():
+        src_iter = ds.batches(vocab, order, a.tokens_per_batch, plan=my_plan, start=start)
+        if a.prefetch > 0:
+            prefetch = Prefetch(((b, atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann, device="cpu"))
+                                 for b in src_iter), a.prefetch)
+            src_iter = prefetch
+        else:
+            src_iter = iter((b, None) for b in src_iter)
+        try:
+            code = _stream(src_iter)
+        finally:
+            if prefetch is not None:
+                prefetch.close()
+    if code is not None:
+        finish_process_group()
+        return
     writer.wait()
     logf.close()
     atlas.check_errors()

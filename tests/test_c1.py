@@ -2,8 +2,8 @@
 pilot, stats v1 + merge loop) — the exactness case, on the real ESM forward.
 
 * CPU (set RUN_SLOW=1; ~10 min): the oracle over the CPU fp32 forward reproduces the reference's
-  own result (tests/golden/c1_esm8m.npz, exact fields compared by sha256), and this build's pilot
-  functions reproduce the reference's edges and seeds on the real activations.
+  own result (tests/golden/c1_esm8m.npz, exact fields compared by sha256), and the oracle's pilot
+  math reproduces the reference's edges and seeds on the real activations.
 * GPU: the same forward on cuda:0, all 512 sequences, feeds the CUDA atlas, the oracle and the
   reference's own Atlas (compiled into oracle/_ref) from the same hook; every exact field must agree
   bit for bit, moments to 1e-6, Gram to 1e-3 Frobenius.
@@ -23,10 +23,16 @@ from tests.harness import as_np, compare, golden, gram_frobenius_rel
 
 
 def _pilot_edges_seeds(Hp, prot, n_total):
-    from proteus_b200.pilot import pilot_edges, pilot_seeds
-    E = torch.cat([pilot_edges([h]) for h in Hp])
-    parts = [pilot_seeds([h], E[li:li + 1], C1["K"], C1["Kr"], n_total, groups=prot) for li, h in enumerate(Hp)]
-    return E.cpu(), torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts])
+    """Edges and seeds: on the device pilot kernels for CUDA activations, the oracle's pilot math
+    (pinned to the reference's) for CPU ones."""
+    if Hp[0].is_cuda:
+        from proteus_b200.pilot import pilot_edges, pilot_seeds
+        E = torch.cat([pilot_edges([h]) for h in Hp])
+        parts = [pilot_seeds([h], E[li:li + 1], C1["K"], C1["Kr"], n_total, groups=prot) for li, h in enumerate(Hp)]
+        return E.cpu(), torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts])
+    E = O.pilot_edges([h.numpy() for h in Hp])
+    ts, rk = O.pilot_seeds([h.numpy() for h in Hp], E, C1["K"], C1["Kr"], n_total, groups=prot.numpy())
+    return torch.from_numpy(E), torch.from_numpy(ts), torch.from_numpy(rk)
 
 
 @pytest.mark.skipif(os.environ.get("RUN_SLOW") != "1", reason="~10 min on 8 cores; set RUN_SLOW=1")

@@ -287,3 +287,49 @@ def test_device_status_clean_after_tensor_core_kernels():
     st = ctypes.c_int(-1)
     assert _lib.load().atlas_device_status(ctypes.byref(st), 0) == 0
     assert st.value == 0
+
+
+# ----------------------------------------------------------------------------------------- pilot
+def test_device_pilot_matches_reference_goldens():
+    """The device pilot (atlas_column_select / _pilot_edges / _pilot_counts / _pilot_seeds) on the
+    reference's pilot inputs (fp32; the second layer rounded to quarters, so edges fall on ties and
+    on signed zeros) equals the reference's pilot_edges / pilot_seeds, with and without protein
+    groups. Edges compare as floats (-0.0 == +0.0: the reference's own sort orders signed zeros
+    arbitrarily, and no bin or threshold can tell them apart); seeds and key ceilings bit for bit."""
+    from proteus_b200.pilot import pilot_edges, pilot_seeds
+    from tests.streams import pilot_inputs
+    Hs, groups = pilot_inputs()
+    z = golden("pilot")
+    Ht = [torch.from_numpy(h).to(DEV) for h in Hs]
+    E = pilot_edges(Ht)
+    assert E.is_cuda and np.array_equal(E.cpu().numpy(), z["E"])
+    ts, rk = pilot_seeds(Ht, E, 16, 8, n_total=10**6, groups=torch.from_numpy(groups))
+    assert np.array_equal(ts.numpy(), z["top_seed"]) and np.array_equal(rk.numpy(), z["res_seed_key"])
+    ts0, rk0 = pilot_seeds(Ht, E, 16, 8, n_total=10**6)
+    assert np.array_equal(ts0.numpy(), z["top_seed_nogroups"]) and np.array_equal(rk0.numpy(), z["res_seed_key_nogroups"])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_device_pilot_matches_oracle_wide_shuffled_groups(dtype):
+    """A wider pilot (n = 20011 rows, D = 1280) in bf16 / fp16 with proteins of random sizes whose
+    ids are not sorted and whose rows are not contiguous: every edge, seed and key ceiling equals the
+    oracle's (pinned to the reference) on the same values."""
+    from oracle import atlas_np as O
+    from proteus_b200.pilot import pilot_edges, pilot_seeds
+    rng = np.random.default_rng(31)
+    n, D = 20011, 1280
+    H = (rng.standard_t(3, (n, D)) * (rng.random(D) + 0.5) + rng.standard_normal(D) * 0.5).astype(np.float32)
+    Hd = torch.from_numpy(H).to(DEV).to(dtype)
+    Hn = Hd.float().cpu().numpy()
+    sizes = rng.integers(1, 400, 200)
+    prot = np.repeat(rng.permutation(10**6)[:200], sizes)[:n]
+    prot = np.concatenate([prot, np.full(n - prot.size, 77)])[rng.permutation(n)]
+    E = pilot_edges([Hd])
+    Eo = O.pilot_edges([Hn])
+    assert np.array_equal(E.cpu().numpy(), Eo)
+    ts, rk = pilot_seeds([Hd], E, 100, 32, n_total=190_000_000, groups=torch.from_numpy(prot))
+    tso, rko = O.pilot_seeds([Hn], Eo, 100, 32, n_total=190_000_000, groups=prot)
+    assert np.array_equal(ts.numpy(), tso) and np.array_equal(rk.numpy(), rko)
+    ts0, rk0 = pilot_seeds([Hd], E, 100, 32, n_total=190_000_000)
+    tso0, rko0 = O.pilot_seeds([Hn], Eo, 100, 32, n_total=190_000_000)
+    assert np.array_equal(ts0.numpy(), tso0) and np.array_equal(rk0.numpy(), rko0)

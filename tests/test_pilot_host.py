@@ -1,5 +1,5 @@
-"""Host-side pieces that need no GPU: pilot edges / seeds against the reference's outputs, the
-dataset batcher, token keys, and the ESM hook plumbing on a tiny CPU model."""
+"""Host-side pieces that need no GPU: the oracle's pilot edges / seeds against the reference's
+outputs, the dataset batcher, token keys, and the ESM hook plumbing on a tiny CPU model."""
 from __future__ import annotations
 
 import numpy as np
@@ -9,17 +9,18 @@ from tests.harness import golden
 from tests.streams import pilot_inputs
 
 
-def test_pilot_edges_and_seeds_match_reference():
-    from proteus_b200.pilot import pilot_edges, pilot_seeds
+def test_oracle_pilot_edges_and_seeds_match_reference():
+    """The oracle's pilot math (the checker of the device pilot) against the reference's own
+    pilot_edges / pilot_seeds outputs, with and without protein groups."""
+    from oracle import atlas_np as O
     Hs, groups = pilot_inputs()
-    Ht = [torch.from_numpy(h) for h in Hs]
     z = golden("pilot")
-    E = pilot_edges(Ht)
-    assert np.array_equal(E.numpy(), z["E"])
-    ts, rk = pilot_seeds(Ht, E, 16, 8, n_total=10**6, groups=torch.from_numpy(groups))
-    assert np.array_equal(ts.numpy(), z["top_seed"]) and np.array_equal(rk.numpy(), z["res_seed_key"])
-    ts0, rk0 = pilot_seeds(Ht, E, 16, 8, n_total=10**6)
-    assert np.array_equal(ts0.numpy(), z["top_seed_nogroups"]) and np.array_equal(rk0.numpy(), z["res_seed_key_nogroups"])
+    E = O.pilot_edges(Hs)
+    assert np.array_equal(E, z["E"])
+    ts, rk = O.pilot_seeds(Hs, E, 16, 8, n_total=10**6, groups=groups)
+    assert np.array_equal(ts, z["top_seed"]) and np.array_equal(rk, z["res_seed_key"])
+    ts0, rk0 = O.pilot_seeds(Hs, E, 16, 8, n_total=10**6)
+    assert np.array_equal(ts0, z["top_seed_nogroups"]) and np.array_equal(rk0, z["res_seed_key_nogroups"])
 
 
 def test_token_keys_and_top_key_match_reference():

@@ -6,6 +6,8 @@ from __future__ import annotations
 
 import json
 
+import pytest
+
 import torch
 
 from proteus_b200.proftrace import attribute, table
@@ -86,3 +88,44 @@ def test_checkpoint_writer_reports_a_failed_write(tmp_path):
     with pytest.raises((FileNotFoundError, RuntimeError), match="does not exist|No such file"):
         w.wait()
     w.wait()  # the error is reported once
+
+
+def test_prefetch_close_joins_a_blocked_producer():
+    """The stream loop may stop with the producer blocked on a full queue or busy on the next item:
+    close() must stop and join it (a producer left inside a torch op at interpreter exit aborts the
+    process)."""
+    import threading
+    import time
+
+    from proteus_b200.run_atlas import Prefetch
+    made = []
+
+    def gen():
+        for i in range(100):
+            made.append(i)
+            yield torch.full((4,), i)
+
+    p = Prefetch(gen(), 2)
+    assert int(next(p)[0]) == 0 and int(next(p)[0]) == 1
+    time.sleep(0.3)  # the producer fills the queue and blocks
+    t0 = time.time()
+    p.close()
+    assert time.time() - t0 < 5 and not any(t.name == "prefetch" and t.is_alive() for t in threading.enumerate())
+    assert len(made) < 10
+
+
+def test_prefetch_reraises_producer_errors_and_ends():
+    from proteus_b200.run_atlas import Prefetch
+
+    def bad():
+        yield 1
+        raise ValueError("broken batch")
+
+    p = Prefetch(bad(), 2)
+    assert next(p) == 1
+    with pytest.raises(ValueError, match="broken batch"):
+        next(p)
+    p.close()
+    q = Prefetch(iter([1, 2]), 1)
+    assert list(q) == [1, 2]
+    q.close()
