@@ -588,6 +588,327 @@ int launch_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int8_t* annT,
   return check_launch("atlas_count_gemm_i8");
 }
 
+// ------------------------------------------------------------------------------------------------
+// Fused subsample statistics + enrichment (bf16 staging): one pass over XT gives the moments and
+// bin counts of atlas_sub_stats AND the enrichment contingencies of atlas_count_gemm_i8, without
+// the int8 masks ever reaching HBM. A CTA owns 128 columns d (the M rows of every mask plane) and a
+// range of 128-row slabs of the subsample:
+//   16 producer warps: 4 threads per column, 32 rows each per slab. Each thread compares its rows
+//     against the column's edges as packed bf16 pairs (exact for bf16 inputs, as atlas_sub_stats),
+//     counts by popcount, sums in fp32 per 8 rows and fp64 across, and writes the 0/1 bytes of every
+//     (pole, level) plane straight into the UMMA K-major 128-byte-swizzled shared-memory tile
+//     (row d, byte i: 16-byte chunk (i / 16) ^ (d % 8)); the annotation one-hots of the slab are
+//     copied into the same layout. A proxy fence and a named barrier later, one thread arrives on
+//     the stage's mbarrier.
+//   1 MMA warp: per slab and plane, four tcgen05.mma kind::i8 (M=128, N=A_pad, K=32) into its own
+//     TMEM accumulator (int32, exact), then a commit that frees the stage.
+//   epilogue: warps 0-3 read the accumulators (lane = column) and add them into enr (int64).
+// Column sums of a CTA range are fp64 partials; with several ranges per column the last CTA to
+// finish (ticket counter) adds the partials in range order, so the result does not depend on CTA
+// timing. Bin counts and contingencies are integers added atomically.
+constexpr int SE_M = 128;
+constexpr int SE_K = 128;
+constexpr int SE_PW = 16;
+constexpr int SE_THREADS = (SE_PW + 1) * 32;
+constexpr int SE_STAGES = 2;
+constexpr int SE_PLANES = 6;
+constexpr int SE_MAXB = 8;
+
+struct SELevels {
+  int v[4];
+};
+
+template <int AP>
+struct SESmem {
+  uint8_t a[SE_STAGES][SE_PLANES][SE_M * SE_K];
+  uint8_t b[SE_STAGES][AP * SE_K];
+  uint64_t full[SE_STAGES], empty[SE_STAGES], tfull;
+  uint32_t tmem_base;
+  int last;
+  int abort;  // a producer's bounded wait gave up: the others skip the remaining slabs too
+};
+
+__device__ __forceinline__ void named_sync_producers() {
+  asm volatile("bar.sync 1, %0;" ::"r"(SE_PW * 32) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 0/1 bytes of 8 rows from the four 32-bit compare masks (0xFFFF per true half) of a vector
+__device__ __forceinline__ uint64_t mask_bytes(const uint32_t (&m)[4]) {
+  return (uint64_t)(__byte_perm(m[0], m[1], 0x6420) & 0x01010101u) |
+         ((uint64_t)(__byte_perm(m[2], m[3], 0x6420) & 0x01010101u) << 32);
+}
+
+template <int AP>
+__global__ void __launch_bounds__(SE_THREADS, 1)
+stats_enrich_kernel(const __nv_bfloat16* __restrict__ XT, int64_t ldx, int64_t col0, int64_t n, int64_t D,
+                    const float* __restrict__ E0, const float* __restrict__ E1, int B, SELevels lev, int NL,
+                    const int8_t* __restrict__ annT, int64_t n_pad, int A, double* __restrict__ sum,
+                    double* __restrict__ sq, unsigned long long* __restrict__ bins, unsigned long long* __restrict__ enr,
+                    double* __restrict__ part, unsigned int* __restrict__ tickets, int spp, int n_slabs,
+                    uint32_t tcols) {
+  extern __shared__ uint8_t se_raw[];
+  SESmem<AP>& s = *reinterpret_cast<SESmem<AP>*>((reinterpret_cast<uintptr_t>(se_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t d0 = (int64_t)blockIdx.x * SE_M;
+  const int k_begin = blockIdx.y * spp;
+  const int k_end = min(n_slabs, k_begin + spp);
+  const int nk = k_end - k_begin;
+  const int planes = 2 * NL;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < SE_STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    mbar_init(&s.tfull, 1);
+    s.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == SE_PW) tmem_alloc(&s.tmem_base, tcols);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  if (warp == SE_PW) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8_s32(SE_M, AP);
+      for (int k = 0; k < nk; ++k) {
+        const int st = k % SE_STAGES;
+        const uint32_t ph = (k / SE_STAGES) & 1;
+        if (!mbar_wait(&s.full[st], ph, 211)) break;
+        tc_fence_after();
+        const uint32_t b_addr = smem_u32(s.b[st]);
+        for (int pl = 0; pl < planes; ++pl) {
+          const uint32_t a_addr = smem_u32(s.a[st][pl]);
+#pragma unroll
+          for (int kk = 0; kk < SE_K / 32; ++kk)
+            mma_i8(tmem + (uint32_t)(pl * AP), sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                   (k == 0 && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(&s.empty[st]);
+      }
+      mma_commit(&s.tfull);
+    }
+  } else {
+    // ---------------------------------------------------------------- producers
+    const int t = threadIdx.x;
+    const int r = t >> 2, prt = t & 3;
+    const int64_t d = d0 + r;
+    const bool dok = d < D;
+    __nv_bfloat162 pe[SE_MAXB], ne[SE_MAXB];
+    int levof[SE_MAXB];  // bit j: level j sits on edge b
+#pragma unroll
+    for (int b = 0; b < SE_MAXB; ++b) {
+      const bool ok = dok && b < B;
+      pe[b] = __bfloat162bfloat162(__float2bfloat16_ru(ok ? E0[d * B + b] : __int_as_float(0x7F800000)));
+      ne[b] = __bfloat162bfloat162(__float2bfloat16_rd(ok ? -E1[d * B + b] : __int_as_float(0xFF800000)));
+      int lm = 0;
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        if (j < NL && lev.v[j] == b) lm |= 1 << j;
+      levof[b] = lm;
+    }
+    int c0[SE_MAXB], c1[SE_MAXB];
+#pragma unroll
+    for (int b = 0; b < SE_MAXB; ++b) c0[b] = c1[b] = 0;
+    double acc_s = 0.0, acc_q = 0.0;
+    const __nv_bfloat16* col = XT + (dok ? d : 0) * ldx + col0;
+    bool ok_run = true;
+    // every producer takes the same nk barrier steps: after a failed wait the shared abort flag
+    // (read after each barrier) turns the remaining steps into no-ops for all of them
+    for (int k = 0; k < nk; ++k) {
+      const int st = k % SE_STAGES;
+      const uint32_t ph = (k / SE_STAGES) & 1;
+      if (ok_run && k >= SE_STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 212)) {
+        ok_run = false;
+        s.abort = 1;
+      }
+      if (ok_run) {
+        const int64_t slab_row0 = (int64_t)(k_begin + k) * SE_K;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = q * 4 + prt;  // 8-row chunk of the slab
+          const int64_t i = slab_row0 + c * 8;
+          uint32_t w4[4] = {0u, 0u, 0u, 0u};
+          uint32_t vm[4] = {0u, 0u, 0u, 0u};
+          if (dok && i < n) {
+            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(col + i));
+            w4[0] = raw.x; w4[1] = raw.y; w4[2] = raw.z; w4[3] = raw.w;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const int64_t rr = i + 2 * w;
+              vm[w] = (rr < n ? 0x0000FFFFu : 0u) | (rr + 1 < n ? 0xFFFF0000u : 0u);
+              w4[w] &= vm[w];
+            }
+            float s32 = 0.0f, q32 = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const float lo = __uint_as_float(w4[w] << 16), hi = __uint_as_float(w4[w] & 0xFFFF0000u);
+              s32 += lo;
+              s32 += hi;
+              q32 = fmaf(lo, lo, q32);
+              q32 = fmaf(hi, hi, q32);
+            }
+            acc_s += (double)s32;
+            acc_q += (double)q32;
+          }
+          uint64_t wp[3] = {0, 0, 0}, wn[3] = {0, 0, 0};
+#pragma unroll
+          for (int b = 0; b < SE_MAXB; ++b) {
+            if (b >= B) break;
+            uint32_t mp[4], mn[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
+              mp[w] = __hge2_mask(h2, pe[b]) & vm[w];
+              mn[w] = __hle2_mask(h2, ne[b]) & vm[w];
+            }
+            c0[b] += __popc(mp[0]) + __popc(mp[1]) + __popc(mp[2]) + __popc(mp[3]);
+            c1[b] += __popc(mn[0]) + __popc(mn[1]) + __popc(mn[2]) + __popc(mn[3]);
+            const int lm = levof[b];
+            if (lm) {
+              const uint64_t bp = mask_bytes(mp), bn = mask_bytes(mn);
+#pragma unroll
+              for (int j = 0; j < 3; ++j)
+                if (lm & (1 << j)) {
+                  wp[j] = bp;
+                  wn[j] = bn;
+                }
+            }
+          }
+          const uint32_t off = (uint32_t)r * 128u + ((uint32_t)((c >> 1) ^ (r & 7)) << 4) + ((uint32_t)(c & 1) << 3);
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            if (j < NL) {
+              *reinterpret_cast<uint64_t*>(s.a[st][j] + off) = wp[j];
+              *reinterpret_cast<uint64_t*>(s.a[st][NL + j] + off) = wn[j];
+            }
+          }
+        }
+        if (t < AP * 8) {  // the slab's annotation one-hots: row a, 16-byte chunk c16
+          const int a_row = t >> 3, c16 = t & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(annT + (int64_t)a_row * n_pad + slab_row0 + c16 * 16);
+          *reinterpret_cast<uint4*>(s.b[st] + a_row * 128 + ((c16 ^ (a_row & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+      }
+      named_sync_producers();
+      ok_run = ok_run && !*reinterpret_cast<volatile int*>(&s.abort);
+      if (t == 0 && ok_run) mbar_arrive(&s.full[st]);
+    }
+    // ---------------------------------------------------------------- column statistics
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      acc_s += __shfl_xor_sync(0xFFFFFFFFu, acc_s, o);
+      acc_q += __shfl_xor_sync(0xFFFFFFFFu, acc_q, o);
+#pragma unroll
+      for (int b = 0; b < SE_MAXB; ++b) {
+        c0[b] += __shfl_xor_sync(0xFFFFFFFFu, c0[b], o);
+        c1[b] += __shfl_xor_sync(0xFFFFFFFFu, c1[b], o);
+      }
+    }
+    if (prt == 0 && dok) {
+#pragma unroll
+      for (int b = 0; b < SE_MAXB; ++b) {
+        if (b >= B) break;
+        const int nx0 = (b + 1 < B) ? c0[b + 1] : 0;
+        const int nx1 = (b + 1 < B) ? c1[b + 1] : 0;
+        const unsigned long long v0 = (unsigned long long)((c0[b] - nx0) >> 4);  // 16 mask bits per row
+        const unsigned long long v1 = (unsigned long long)((c1[b] - nx1) >> 4);
+        if (v0) atomicAdd(bins + d * B + b, v0);
+        if (v1) atomicAdd(bins + (D + d) * B + b, v1);
+      }
+      if (gridDim.y == 1) {
+        sum[d] += acc_s;
+        sq[d] += acc_q;
+      } else {
+        part[((int64_t)blockIdx.y * 2) * D + d] = acc_s;
+        part[((int64_t)blockIdx.y * 2 + 1) * D + d] = acc_q;
+      }
+    }
+    // ---------------------------------------------------------------- contingencies
+    if (warp < 4 && nk > 0 && mbar_wait(&s.tfull, 0, 213)) {
+      tc_fence_after();
+      const int64_t dd = d0 + warp * 32 + lane;
+      for (int pl = 0; pl < planes; ++pl) {
+        const int pole = pl / NL, j = pl - pole * NL;
+#pragma unroll
+        for (int c = 0; c < AP; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(pl * AP + c), v);
+          tmem_ld_wait();
+          if (dd < D) {
+            unsigned long long* row = enr + (((int64_t)pole * NL + j) * D + dd) * A;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              if (c + jj < A && v[jj]) atomicAdd(row + c + jj, (unsigned long long)v[jj]);
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+  // ---------------------------------------------------------------- ordered sum of the range partials
+  if (gridDim.y > 1) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned int ticket = atomicAdd(tickets + blockIdx.x, 1u);
+      s.last = ticket == gridDim.y - 1;
+    }
+    __syncthreads();
+    if (s.last) {
+      __threadfence();
+      if (threadIdx.x < SE_M) {
+        const int64_t d = d0 + threadIdx.x;
+        if (d < D) {
+          double S = 0.0, Q = 0.0;
+          for (unsigned int y = 0; y < gridDim.y; ++y) {
+            S += __ldcg(part + ((int64_t)y * 2) * D + d);
+            Q += __ldcg(part + ((int64_t)y * 2 + 1) * D + d);
+          }
+          sum[d] += S;
+          sq[d] += Q;
+        }
+      }
+      if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
+    }
+  }
+  __syncthreads();
+  if (warp == SE_PW) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tcols);
+  }
+}
+
+template <int AP>
+int launch_stats_enrich(const __nv_bfloat16* XT, int64_t ldx, int64_t col0, int64_t n, int64_t D, const float* E0,
+                        const float* E1, int B, const SELevels& lev, int NL, const int8_t* annT, int64_t n_pad, int A,
+                        double* sum, double* sq, int64_t* bins, int64_t* enr, void* ws, cudaStream_t st) {
+  const int n_slabs = (int)((n + SE_K - 1) / SE_K);
+  const int dtiles = (int)((D + SE_M - 1) / SE_M);
+  int ks = num_sms() / dtiles;
+  ks = ks < 1 ? 1 : (ks > 16 ? 16 : ks);
+  if (ks > n_slabs) ks = n_slabs;
+  const int spp = (n_slabs + ks - 1) / ks;
+  ks = (n_slabs + spp - 1) / spp;  // every range gets at least one slab
+  unsigned int* tickets = reinterpret_cast<unsigned int*>(ws);
+  double* part = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(ws) + ((dtiles * 4 + 255) / 256) * 256);
+  const size_t smem = sizeof(SESmem<AP>) + 1024;
+  if (cudaFuncSetAttribute(stats_enrich_kernel<AP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return fail(ATLAS_ERR_CUDA, "sub_stats_enrich: cannot reserve %zu bytes of shared memory", smem);
+  uint32_t tcols = 32;
+  while (tcols < (uint32_t)(2 * NL * AP)) tcols <<= 1;
+  stats_enrich_kernel<AP><<<dim3((unsigned)dtiles, (unsigned)ks), SE_THREADS, smem, st>>>(
+      XT, ldx, col0, n, D, E0, E1, B, lev, NL, annT, n_pad, A, sum, sq, reinterpret_cast<unsigned long long*>(bins),
+      reinterpret_cast<unsigned long long*>(enr), part, tickets, spp, n_slabs, tcols);
+  return check_launch("atlas_sub_stats_enrich");
+}
+
 }  // namespace
 
 // fp32 activations keep an exact-FMA CUDA-core Gram (tcgen05 has no IEEE fp32 operand kind)
@@ -695,5 +1016,50 @@ extern "C" int atlas_count_gemm_i8(const int8_t* masks, int64_t M, int64_t n_pad
     case 128: return launch_i8<128>(masks, M, n_pad, annT, out, A, st);
     case 256: return launch_i8<256>(masks, M, n_pad, annT, out, A, st);
     default: return fail(ATLAS_ERR_UNSUPPORTED, "count_gemm_i8: A_pad %lld not instantiated", (long long)A_pad);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Fused subsample statistics + enrichment (see stats_enrich_kernel).
+extern "C" int atlas_stats_enrich_supported(int dtype, int64_t B, int64_t NL, int64_t A_pad) {
+  return dtype == ATLAS_BF16 && B >= 1 && B <= SE_MAXB && NL >= 1 && NL <= 3 && (A_pad == 16 || A_pad == 32 ||
+                                                                               A_pad == 48);
+}
+
+extern "C" int64_t atlas_stats_enrich_ws_bytes(int64_t D, int64_t n) {
+  if (D <= 0) return 256;
+  const int64_t dtiles = (D + SE_M - 1) / SE_M;
+  return ((dtiles * 4 + 255) / 256) * 256 + 16 * 2 * D * 8;
+}
+
+extern "C" int atlas_sub_stats_enrich(const void* XT, int dtype, int64_t ldx, int64_t col0, int64_t n, int64_t D,
+                                      const float* E0, const float* E1, int64_t B, const int32_t* levels_host,
+                                      int64_t NL, double* sum, double* sq, int64_t* bins, const int8_t* annT,
+                                      int64_t A_pad, int64_t n_pad, int64_t* enr, int64_t A, void* ws,
+                                      int64_t ws_bytes, void* stream) {
+  ATLAS_REQUIRE(atlas_stats_enrich_supported(dtype, B, NL, A_pad),
+                "sub_stats_enrich: unsupported (bf16 staging, 1..%d bins, 1..3 levels, A_pad 16/32/48 only)", SE_MAXB);
+  ATLAS_REQUIRE(n >= 0 && D >= 0 && A >= 1 && A <= A_pad, "sub_stats_enrich: bad sizes");
+  if (n == 0 || D == 0) return ATLAS_OK;
+  ATLAS_REQUIRE(XT && E0 && E1 && sum && sq && bins && annT && enr && ws && levels_host, "sub_stats_enrich: null pointer");
+  ATLAS_REQUIRE(col0 % 8 == 0 && ldx % 8 == 0 && (col0 + ((n + 7) / 8) * 8) <= ldx && (uintptr_t)XT % 16 == 0,
+                "sub_stats_enrich: XT must be 16-byte aligned, col0 and ldx multiples of 8, columns inside ldx");
+  ATLAS_REQUIRE(n_pad % 128 == 0 && n_pad >= n && (uintptr_t)annT % 16 == 0, "sub_stats_enrich: n_pad %% 128 == 0, >= n");
+  ATLAS_REQUIRE(ws_bytes >= atlas_stats_enrich_ws_bytes(D, n), "sub_stats_enrich: workspace too small");
+  ATLAS_REQUIRE(D < (1LL << 31), "sub_stats_enrich: D too large");
+  SELevels lev{};
+  for (int j = 0; j < NL; ++j) {
+    ATLAS_REQUIRE(levels_host[j] >= 0 && levels_host[j] < B, "sub_stats_enrich: level %d out of range", j);
+    lev.v[j] = levels_host[j];
+  }
+  const auto* x = reinterpret_cast<const __nv_bfloat16*>(XT);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (A_pad) {
+    case 16: return launch_stats_enrich<16>(x, ldx, col0, n, D, E0, E1, (int)B, lev, (int)NL, annT, n_pad, (int)A, sum,
+                                            sq, bins, enr, ws, st);
+    case 32: return launch_stats_enrich<32>(x, ldx, col0, n, D, E0, E1, (int)B, lev, (int)NL, annT, n_pad, (int)A, sum,
+                                            sq, bins, enr, ws, st);
+    default: return launch_stats_enrich<48>(x, ldx, col0, n, D, E0, E1, (int)B, lev, (int)NL, annT, n_pad, (int)A, sum,
+                                            sq, bins, enr, ws, st);
   }
 }

@@ -191,13 +191,15 @@ def test_c4_prefix_dual_sink_matches_reference_atlas():
         assert vo[k] == vr[k], (k, vo[k], vr[k])
     assert ours.stats["dense_layer_batches"] == ref.stats["redo_layers"] == redo_total
     check_moments(as_np(ours.sub_sum), as_np(ours.sub_sq), as_np(ref.sub_sum), as_np(ref.sub_sq), ref.n_sub, "C4")
-    # Gram, layer by layer on the device (upper block triangle: both keep the lower blocks at zero)
+    # Gram, layer by layer on the device, upper triangles: stats v1 of the reference accumulates the
+    # whole X^T X, this build (like the reference's v3) the upper block triangle; result() makes
+    # both symmetric from the upper triangle (symmetrize_upper, atlas/core.py:756-759)
     ours.flush_gram()
     ref.flush_gram()
     assert ours.gram_rows == ref.gram_rows
     worst = 0.0
     for l in range(L):
-        a, r = ours.gram64[l], ref.gram64[l].to(dev)
+        a, r = torch.triu(ours.gram64[l]), torch.triu(ref.gram64[l].to(dev))
         worst = max(worst, float(torch.linalg.norm(a - r) / torch.linalg.norm(r)))
     print(f"C4 Gram: worst layer relative Frobenius error {worst:.3g}; reference dense redo layer-batches {redo_total}")
     assert worst < 1e-3
