@@ -337,8 +337,7 @@ def kernel_microbench(dev, peaks, reps=20):
     ms = timed(lambda: KN.sub_stats_into(XT, 0, n, E0, E1, levels, s_, sq_, bins_, masks, n))
     bytes_ = D * n * 2 + 2 * NL * D * n + D * (2 * B * 4 + 2 * 8 * 2 + 2 * B * 8 * 2)
     out["stats_c3"] = {"D": D, "rows_per_call": n, "ms_per_call": ms, "bytes": bytes_, "GBps": bytes_ / ms / 1e6,
-                       "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"]}
-    del XT
+                       "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"], "path": "atlas_sub_stats (masks to HBM)"}
     # C3 int8 enrichment GEMM: masks [2*3*D, 16384] x one-hot labels [32, 16384] (Zipf s=1.1 classes)
     A = 32
     zipf = 1.0 / torch.arange(1, A + 1, device=dev, dtype=torch.float64) ** 1.1
@@ -354,6 +353,19 @@ def kernel_microbench(dev, peaks, reps=20):
     out["i8_c3"] = {"M": M, "K": n, "N": A, "ms_per_call": ms, "TOPs": ops / ms / 1e9, "bytes": bytes_,
                     "GBps": bytes_ / ms / 1e6, "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"]}
     del masks, m2, cnt_out
+    # C3 statistics + enrichment fused (atlas_sub_stats_enrich): one read of the staged rows, masks
+    # built in shared memory for the int8 tensor-core contraction; algorithmic bytes = the staged
+    # rows (n x D x 2) + the one-hot tile + the per-column outputs
+    ws = KN.StatsEnrichWorkspace(dev)
+    enr = torch.zeros(M, A, device=dev, dtype=torch.int64)
+    ms = timed(lambda: KN.sub_stats_enrich_into(XT, 0, n, E0, E1, levels, s_, sq_, bins_, annT, enr, A, ws))
+    bytes_ = D * n * 2 + A * n + D * (2 * B * 4 + 2 * 8 * 2 + 2 * B * 8 * 2) + M * A * 8 * 2
+    out["stats_enrich_c3"] = {"D": D, "rows_per_call": n, "A": A, "levels": levels, "ms_per_call": ms, "bytes": bytes_,
+                              "GBps": bytes_ / ms / 1e6, "frac_hbm": bytes_ / ms / 1e6 / peaks["hbm_gbs"],
+                              "two_kernel_ms": out["stats_c3"]["ms_per_call"] + out["i8_c3"]["ms_per_call"],
+                              "TOPs": 2 * M * n * A / ms / 1e9}
+    del XT, enr
+    out["dense_c4"] = dense_burst(dev, peaks, scale, shift)
     # C2 top-K merge: one block's candidates (~0.2% of 16384 x 5120, random keys) into the [10240, 100]
     # state of one layer (2 poles x 5120 columns), sorted rows, fresh candidates every call
     G, K = 2 * D, 100
@@ -378,6 +390,45 @@ def kernel_microbench(dev, peaks, reps=20):
     del st_sc, st_tok, st_val, sets
     out["c2_stream"] = c2_stream(dev, peaks, scale, shift)
     return out
+
+
+@torch.no_grad()
+def dense_burst(dev, peaks, scale, shift, T=32768, D=5120, reps=6):
+    """The dense burst path at C4 shapes: one layer of [32768 x 5120] bf16 (Student-t(3) x scale +
+    shift, 8% padding rows), K=100, Kr=32, 5 bins, forced dense in every batch (naive mode), as an
+    overflowed layer takes it. Times atlas_dense_select (the valid-row gather and the per-column
+    exact top-K and per-bin bottom-Kr) with CUDA events per launch; reports ms per layer-batch, the
+    activation bytes it consumes per second and GB/s against ~4 passes over n_v x D x 2 bytes."""
+    from proteus_b200.core import Atlas, AtlasConfig
+    g = torch.Generator(device=dev).manual_seed(29)
+    qs = torch.tensor([0.5, 0.9, 0.99, 0.999, 0.9999], device=dev)
+    H = (torch.distributions.StudentT(torch.tensor(3.0, device=dev)).sample((T, D)) * scale + shift).to(torch.bfloat16)
+    E = torch.stack([torch.quantile(H[:4096].float(), qs, dim=0).T, torch.quantile(-H[:4096].float(), qs, dim=0).T])
+    at = Atlas(1, D, E.unsqueeze(0).contiguous(), AtlasConfig(K=100, Kr=32, seed=0, subsample=False, gram=False,
+                                                             naive=True), device=dev)
+    Lmax = 256
+    valid = torch.cat([r * Lmax + 1 + torch.arange(Lmax - 2 - (r % 37)) for r in range(T // Lmax)])
+    kt = KernelTimer()
+    n_v = valid.numel()
+    for i in range(reps + 2):
+        seq = torch.div(valid, Lmax, rounding_mode="floor") + (T // Lmax) * i
+        tok = seq * 1024 + (valid % Lmax) - 1
+        ctx = at.make_ctx(T, valid, tok)
+        at.kernel_timer = kt if i >= 2 else None
+        at.begin_batch(ctx)
+        at.observe(0, H)
+        at.end_batch()
+    torch.cuda.synchronize()
+    at.check_errors()
+    ms = kt.total_ms("dense") / max(1, kt.count("dense"))
+    h_bytes = n_v * D * 2
+    res = {"layer_batches": kt.count("dense"), "valid_rows": n_v, "D": D, "K": 100, "Kr": 32,
+           "ms_per_layer_batch": ms, "H_GBps": h_bytes / ms / 1e6,
+           "GBps_4_passes": 4 * h_bytes / ms / 1e6, "frac_hbm_4_passes": 4 * h_bytes / ms / 1e6 / peaks["hbm_gbs"],
+           "dense_layer_batches": at.stats["dense_layer_batches"]}
+    del H, at
+    torch.cuda.empty_cache()
+    return res
 
 
 @torch.no_grad()
@@ -836,6 +887,9 @@ def main():
                              "peak_source": peaks["source"]},
                 "gram_staged": {"launches": kt.count("gram"), "ms_total": kt.total_ms("gram"),
                                 "rows": kt.work.get("gram", 0)},
+                "dense_in_step": {"launches": kt.count("dense"), "ms_total": kt.total_ms("dense"),
+                                  "triggered_layer_batches": stats1["dense_layer_batches"] - stats0.get("dense_layer_batches", 0)},
+                "device_status": atlas.device_status(),
                 "gpu_launches": launches, "clocks": clk, "setup_s": setup_s,
                 "combine_ms": combine_ms,
                 "stats_delta": {k: stats1[k] - stats0.get(k, 0) for k in stats1}}

@@ -111,6 +111,26 @@ int atlas_count_gemm_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int
                         int64_t* out, int64_t A, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Subsample statistics and enrichment in one pass — replaces sub_stats followed by _count_mm_i8
+ * (atlas/stats_triton.py:77-117, atlas/core.py:378-399, :762-774) without materialising the int8
+ * masks: the same accumulations as atlas_sub_stats (sum, sq, bins; masks are not written) and as
+ * atlas_count_gemm_i8 on those masks (enr [2, NL, D, A] int64 += masks . annT^T), read from XT once.
+ * The 0/1 mask tiles are built in shared memory and contracted on tcgen05 (kind::i8, exact int32).
+ * Supported when atlas_stats_enrich_supported(dtype, B, NL, A_pad) != 0 (bf16 staging, B <= 8,
+ * 1 <= NL <= 3, A_pad in {16, 32, 48}); otherwise use the two kernels. annT [A_pad, n_pad] int8
+ * (n_pad % 128 == 0, zero past the n subsample rows). ws: device workspace of
+ * atlas_stats_enrich_ws_bytes(D, n) bytes, zero-filled before its first use (the kernel leaves it
+ * reusable); calls sharing one ws must not overlap. Sums are fp32 per 8 rows and fp64 across, in
+ * an order that does not depend on CTA timing.
+ */
+int atlas_stats_enrich_supported(int dtype, int64_t B, int64_t NL, int64_t A_pad);
+int64_t atlas_stats_enrich_ws_bytes(int64_t D, int64_t n);
+int atlas_sub_stats_enrich(const void* XT, int dtype, int64_t ldx, int64_t col0, int64_t n, int64_t D,
+                           const float* E0, const float* E1, int64_t B, const int32_t* levels_host, int64_t NL,
+                           double* sum, double* sq, int64_t* bins, const int8_t* annT, int64_t A_pad, int64_t n_pad,
+                           int64_t* enr, int64_t A, void* ws, int64_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Upper-block-triangle Gram on tcgen05 tensor cores — replaces gram_accumulate
  * (atlas/stats_triton.py:148-169): C[D, D] (fp32, row-major, contiguous) += X^T X on the 128x128
  * blocks with block row <= block column; lower blocks untouched. X is supplied transposed:

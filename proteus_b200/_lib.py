@@ -80,7 +80,8 @@ def load(path: str | os.PathLike | None = None):
 
 
 # kernels launched per call (predicated kernels that exit early on the device still count)
-_KERNELS = {"atlas_grouped_merge": 6, "atlas_last_error": 0, "atlas_abi_version": 0}
+_KERNELS = {"atlas_grouped_merge": 6, "atlas_last_error": 0, "atlas_abi_version": 0, "atlas_device_status": 0,
+            "atlas_device_status_set": 0, "atlas_stats_enrich_supported": 0}
 LAUNCHES = {"count": 0}
 
 

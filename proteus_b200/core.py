@@ -10,7 +10,8 @@ What runs where (all compute is the sm_100a library; there is no CPU path):
   begin_batch  atlas_thresholds                      (core.py:250-259)
   observe      atlas_filter_compact                  (K1, filter_triton.py)
                atlas_gather_transpose / _rows        (subsample rows -> transposed staging / bulk rows)
-               atlas_sub_stats, atlas_count_gemm_i8  (moments, bin masses, enrichment; core.py:312-404)
+               atlas_sub_stats_enrich                (moments, bin masses, enrichment in one pass;
+                                                     or atlas_sub_stats + atlas_count_gemm_i8; core.py:312-404)
                atlas_gram_upper                      (upper-block Gram over staged subsample rows)
                atlas_dense_select                    (_dense, core.py:407-446), run on the device only
                                                      when the layer is dense or its buffer overflowed
@@ -250,6 +251,7 @@ class Atlas:
         self._act_dtype = None
         self._ws_top = KN.MergeWorkspace(dev)
         self._ws_res = KN.MergeWorkspace(dev)
+        self._ws_se = KN.StatsEnrichWorkspace(dev)
         self._cap_cache = None
         self.kernel_timer = None  # optional object with start(name) / stop(name) around kernel launches
 
@@ -413,7 +415,11 @@ class Atlas:
         c = self.cfg
         fl = self._flags
         with _rf("atlas.dense"):
+            if kt is not None:
+                kt.start("dense")
             self._dense_call(H, dt, T, D, l, ctx, c, cap, dense, tg, tsc, tt, tv, tcap, rg, rsc, rt, rv, rcap, fl, st)
+            if kt is not None:
+                kt.stop("dense", work=ctx.n_v if dense else 0)
         self._pending[l] = "dense" if dense else "filtered"
 
     def _dense_call(self, H, dt, T, D, l, ctx, c, cap, dense, tg, tsc, tt, tv, tcap, rg, rsc, rt, rv, rcap, fl, st):
@@ -451,6 +457,18 @@ class Atlas:
         KN.gather_transpose(H, ctx.sub_rows32, XT, col0)
         levels = list(self.cfg.enrich_levels)
         ann = bool(self.n_a) and ctx.annT is not None and len(levels) > 0
+        if ann and KN.stats_enrich_supported(XT.dtype, self.B, len(levels), ctx.annT.shape[0]):
+            # one pass over the staged rows: moments, bin masses and the enrichment contingencies,
+            # the 0/1 masks built in shared memory for the int8 tensor-core contraction
+            with _rf("atlas.sub.kernel"):
+                KN.sub_stats_enrich_into(XT, col0, n, self.E[l, 0], self.E[l, 1], levels, self.sub_sum[l],
+                                         self.sub_sq[l], self.sub_bin[l], ctx.annT,
+                                         self.enr[l].view(2 * len(levels) * D, self.n_a), self.n_a, self._ws_se)
+            if self.gram is not None:
+                self._stage_fill[l] += n8
+                if l == 0:
+                    self.gram_rows += n
+            return
         n_pad = ctx.annT.shape[1] if ann else _ceil(n, 8)
         masks = None
         if ann:

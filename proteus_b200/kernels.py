@@ -70,6 +70,39 @@ def sub_stats_into(XT, col0, n, E0, E1, levels, sum_, sq, bins, masks, n_pad):
          ptr(masks) if NL else None, int(n_pad), stream_ptr(XT.device))
 
 
+def stats_enrich_supported(dtype, B: int, NL: int, A_pad: int) -> bool:
+    return bool(_lib.load().atlas_stats_enrich_supported(dtype_code(dtype), B, NL, A_pad))
+
+
+class StatsEnrichWorkspace:
+    """Zero-filled device workspace of atlas_sub_stats_enrich (range partials of the column sums and
+    per-column-tile tickets), grown on demand."""
+
+    def __init__(self, device):
+        self.device = device
+        self.buf = None
+
+    def get(self, D: int, n: int) -> torch.Tensor:
+        need = int(_lib.load().atlas_stats_enrich_ws_bytes(D, n))
+        if self.buf is None or self.buf.numel() < need:
+            self.buf = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def sub_stats_enrich_into(XT, col0, n, E0, E1, levels, sum_, sq, bins, annT, enr, A, ws: StatsEnrichWorkspace):
+    """Fused atlas_sub_stats_enrich over XT[:, col0:col0+n]: moments and bin masses of the columns
+    and the enrichment contingencies enr [2*NL*D, A] += masks . annT^T, masks never materialised."""
+    import ctypes
+    D = XT.shape[0]
+    B = E0.shape[1]
+    NL = len(levels)
+    lev = (ctypes.c_int32 * NL)(*levels)
+    w = ws.get(D, n)
+    call("atlas_sub_stats_enrich", ptr(XT), dtype_code(XT.dtype), XT.stride(0), int(col0), int(n), D, ptr(E0), ptr(E1),
+         B, ctypes.cast(lev, ctypes.c_void_p), NL, ptr(sum_), ptr(sq), ptr(bins), ptr(annT), annT.shape[0],
+         annT.shape[1], ptr(enr), int(A), ptr(w), w.numel(), stream_ptr(XT.device))
+
+
 def sub_stats(X, E0, E1, levels, **_tile):
     """Drop-in for stats_triton.sub_stats (stats_triton.py:77-117): X [n, D] (unit column stride);
     returns (sum fp64 [D], sumsq fp64 [D], counts int32 [2, D, B], masks int8 [2, NL, D, n8])."""

@@ -333,3 +333,58 @@ def test_device_pilot_matches_oracle_wide_shuffled_groups(dtype):
     ts0, rk0 = pilot_seeds([Hd], E, 100, 32, n_total=190_000_000)
     tso0, rko0 = O.pilot_seeds([Hn], Eo, 100, 32, n_total=190_000_000)
     assert np.array_equal(ts0.numpy(), tso0) and np.array_equal(rk0.numpy(), rko0)
+
+
+# ----------------------------------------------------------------------------------------- fused stats + enrichment
+@pytest.mark.parametrize("D,n,A,NL,col0", [(1333, 1611, 21, 3, 64), (5120, 16384, 32, 3, 0), (300, 300, 7, 2, 8),
+                                           (257, 129, 48, 1, 0), (640, 9000, 16, 3, 24)])
+def test_stats_enrich_fused_equals_two_kernel_path(D, n, A, NL, col0):
+    """atlas_sub_stats_enrich (masks built in shared memory, int8 tcgen05 contraction) against
+    atlas_sub_stats (masks written to HBM) + atlas_count_gemm_i8 on the same staged rows: bin masses
+    and contingencies bit-exact, moments to 1e-12 of the column mass (both sum fp32 per 8 rows and
+    fp64 across, in different fp64 orders). Ragged D (not a multiple of 128), ragged n, an offset
+    staging column, multi-hot annotation rows; called twice (accumulation, reused workspace)."""
+    from proteus_b200 import kernels as KN
+    g = torch.Generator(device=DEV).manual_seed(D + n)
+    B, levels = 5, [2, 3, 4][:NL] if NL > 1 else [3]
+    t = torch.randn(n, D, device=DEV, generator=g) / torch.sqrt((torch.randn(n, D, device=DEV, generator=g) ** 2
+                                                                 + torch.randn(n, D, device=DEV, generator=g) ** 2) / 2)
+    X = (t * (torch.rand(D, device=DEV, generator=g) + 0.5) + torch.randn(D, device=DEV, generator=g) * 0.5)
+    X = X.to(torch.bfloat16)
+    qs = torch.tensor([0.5, 0.9, 0.99, 0.999, 0.9999], device=DEV)
+    E0 = torch.quantile(X[:4096].float(), qs, dim=0).T.contiguous()
+    E1 = torch.quantile(-X[:4096].float(), qs, dim=0).T.contiguous()
+    ldx = col0 + ((n + 63) // 64) * 64 + 64
+    XT = torch.full((D, ldx), float("nan"), device=DEV, dtype=torch.bfloat16)  # garbage outside the rows
+    KN.gather_transpose(X, torch.arange(n, dtype=torch.int32, device=DEV), XT, col0)
+    A_pad = max(16, -(-A // 16) * 16)
+    n_pad = max(128, -(-n // 128) * 128)
+    annT = torch.zeros(A_pad, n_pad, dtype=torch.int8, device=DEV)
+    lab = torch.randint(0, A, (n, 3), device=DEV, generator=g)
+    keep = torch.rand(n, 3, device=DEV, generator=g) < torch.tensor([1.0, 0.4, 0.2], device=DEV)
+    for c in range(3):
+        rows = torch.nonzero(keep[:, c]).squeeze(1)
+        annT[lab[rows, c], rows] = 1
+    assert KN.stats_enrich_supported(torch.bfloat16, B, NL, A_pad)
+    want = [torch.zeros(D, dtype=torch.float64, device=DEV), torch.zeros(D, dtype=torch.float64, device=DEV),
+            torch.zeros(2, D, B, dtype=torch.int64, device=DEV), torch.zeros(2 * NL * D, A, dtype=torch.int64, device=DEV)]
+    got = [torch.zeros_like(x) for x in want]
+    masks = torch.zeros(2 * NL * D * n_pad, dtype=torch.int8, device=DEV)
+    ws = KN.StatsEnrichWorkspace(DEV)
+    M = 2 * NL * D
+    M_pad = -(-M // 128) * 128
+    mpad = torch.zeros(M_pad * n_pad, dtype=torch.int8, device=DEV)
+    for _ in range(2):
+        KN.sub_stats_into(XT, col0, n, E0, E1, levels, want[0], want[1], want[2], masks, n_pad)
+        mpad[:M * n_pad].copy_(masks)
+        out = torch.zeros(M_pad, A, dtype=torch.int64, device=DEV)
+        KN.count_gemm_i8(mpad.view(M_pad, n_pad), annT, out, A)
+        want[3] += out[:M]
+        KN.sub_stats_enrich_into(XT, col0, n, E0, E1, levels, got[0], got[1], got[2], annT, got[3], A, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(got[2], want[2]), "bin masses differ"
+    assert torch.equal(got[3], want[3]), f"contingencies differ in {int((got[3] != want[3]).sum())} entries"
+    mass = torch.sqrt(n * want[1]) + 1e-300
+    assert bool(((got[0] - want[0]).abs() <= 1e-12 * mass).all())
+    assert bool(((got[1] - want[1]).abs() <= 1e-12 * want[1]).all())
+    assert int(want[3].sum()) > 0
