@@ -61,6 +61,30 @@ int atlas_filter_compact(const void* H, int dtype, int64_t T, int64_t D, int64_t
                          int64_t cap, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
+ * Batch context on the device — replaces the row-level decisions of Atlas.make_ctx
+ * (atlas/core.py:210-237), so a batch needs only its raw valid rows, token ids and annotation ids.
+ * atlas_ctx_rows: valid_rows int64 [n_v] (rows of H, < T), tok int64 [n_v] (in [0, 2^32); a bad one
+ *   sets *err and is skipped). Writes key int64 [n_v] = lowbias32((tok ^ seed) mod 2^32)
+ *   (core.py:46-55); rowmap int32 [T] (-1 for padding rows); the subsample {i : key < U_sub} in
+ *   increasing i as sub_idx int64 and sub_rows32 = valid_rows[sub_idx]; within it the bulk rows
+ *   {j : key[sub_idx[j]] < U_res} as res_in_sub int64 (positions j), res_rows32 and res_vidx32
+ *   (valid index); key_order int32 [n_v] = valid indices by ascending key; counts int64 [2] =
+ *   (n_s, n_r), on the device. Index outputs are sized n_v (the first n_s / n_r entries are set).
+ *   ws: device bytes >= atlas_ctx_ws_bytes(n_v). Asynchronous on `stream`.
+ * atlas_ctx_annotations: ann int64 [n_v, m_a] (class ids, -1 padded); writes annT int8
+ *   [A_pad, n_pad] with annT[a, j] = 1 when a is among the ids of subsample row j (zero elsewhere;
+ *   n_pad >= n_s) and ann_totals int64 [n_a] = per-class row counts of the subsample (the
+ *   ann_sub / ann_sub_i8 of the reference's make_ctx, transposed for the enrichment contraction).
+ */
+int64_t atlas_ctx_ws_bytes(int64_t n_v);
+int atlas_ctx_rows(const int64_t* valid_rows, const int64_t* tok, int64_t n_v, int64_t T, int64_t seed, int64_t U_sub,
+                   int64_t U_res, int64_t* key, int32_t* rowmap, int64_t* sub_idx, int64_t* res_in_sub,
+                   int32_t* sub_rows32, int32_t* res_rows32, int32_t* res_vidx32, int32_t* key_order, int64_t* counts,
+                   int32_t* err, void* ws, int64_t ws_bytes, void* stream);
+int atlas_ctx_annotations(const int64_t* sub_idx, const int64_t* counts, const int64_t* ann, int64_t n_v, int64_t m_a,
+                          int64_t n_a, int8_t* annT, int64_t A_pad, int64_t n_pad, int64_t* ann_totals, void* stream);
+
+/* ------------------------------------------------------------------------------------------------
  * Per-batch compaction thresholds — replaces the device math of Atlas.begin_batch
  * (atlas/core.py:250-259):
  *   tau_top = max(nextafter(top_s[g, K-1], -inf), top_seed[g])

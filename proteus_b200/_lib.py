@@ -85,6 +85,9 @@ _KERNELS = {"atlas_grouped_merge": 6, "atlas_last_error": 0, "atlas_abi_version"
 LAUNCHES = {"count": 0}
 
 
+_KERNELS.update({"atlas_ctx_rows": 4, "atlas_ctx_annotations": 2})
+
+
 def _n_kernels(name: str, args) -> int:
     if name == "atlas_dense_select":
         return 3 if args[14] else 1

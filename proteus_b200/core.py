@@ -160,6 +160,7 @@ class BatchCtx:
     key_order32: torch.Tensor | None = None  # [n_v] valid indices by ascending key
     annT: torch.Tensor | None = None         # [A_pad, n_pad] int8 one-hots, transposed
     ann_counts: torch.Tensor | None = None   # [n_a] int64 column sums of ann_sub
+    ready: object = None                     # CUDA event: the context's tensors are complete (device make_ctx)
 
     def to(self, device, non_blocking: bool = False) -> "BatchCtx":
         mv = lambda t: None if t is None else t.to(device, non_blocking=non_blocking)  # noqa: E731
@@ -309,6 +310,60 @@ class Atlas:
                        key_order32=torch.argsort(key).to(torch.int32), annT=annT, ann_counts=ann_counts)
         return ctx if d.type == "cpu" else ctx.to(d)
 
+    @torch.no_grad()
+    def make_ctx_device(self, T: int, valid_rows, tok, ann_ids=None, stream=None) -> BatchCtx:
+        """make_ctx on the device (atlas_ctx_rows / atlas_ctx_annotations): the same row-level
+        decisions as make_ctx (core.py:210-237) from the batch's raw valid rows, token ids and
+        annotation ids (host tensors, pinned for an asynchronous copy, or device tensors). Runs on
+        `stream` (default: the current stream); only that stream is waited on, for the two counts
+        (n_s, n_r) the host needs to size the batch's launches, so a prefetch thread can build the
+        next context on a side stream while the main stream works. The context's `ready` event is
+        waited on by begin_batch."""
+        dev = self.dev
+        st = stream if stream is not None else torch.cuda.current_stream(dev)
+        with torch.cuda.device(dev), torch.cuda.stream(st):
+            vr = torch.as_tensor(valid_rows).to(dev, torch.int64, non_blocking=True)
+            tk = torch.as_tensor(tok).to(dev, torch.int64, non_blocking=True)
+            n_v = vr.numel()
+            i64 = dict(dtype=torch.int64, device=dev)
+            i32 = dict(dtype=torch.int32, device=dev)
+            key, sub_idx, res_in_sub = torch.empty(n_v, **i64), torch.empty(n_v, **i64), torch.empty(n_v, **i64)
+            rowmap32 = torch.empty(T, **i32)
+            sub_rows32, res_rows32, res_vidx32 = torch.empty(n_v, **i32), torch.empty(n_v, **i32), torch.empty(n_v, **i32)
+            key_order32 = torch.empty(n_v, **i32)
+            counts = torch.zeros(2, **i64)
+            err = torch.zeros(1, **i32)
+            ws = torch.empty(int(load().atlas_ctx_ws_bytes(n_v)), dtype=torch.uint8, device=dev)
+            call("atlas_ctx_rows", ptr(vr), ptr(tk), n_v, T, self.cfg.seed, self.U_sub, self.U_res, ptr(key),
+                 ptr(rowmap32), ptr(sub_idx), ptr(res_in_sub), ptr(sub_rows32), ptr(res_rows32), ptr(res_vidx32),
+                 ptr(key_order32), ptr(counts), ptr(err), ptr(ws), ws.numel(), st.cuda_stream)
+            host = torch.empty(3, dtype=torch.int64, pin_memory=True)
+            host[:2].copy_(counts, non_blocking=True)
+            host[2:].copy_(err, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(st)
+            done.synchronize()  # this stream only: the counts size the views below
+            n_s, n_r, bad = (int(x) for x in host.tolist())
+            if bad:
+                raise ValueError("token ids must be in [0, 2^32) and valid rows inside the batch")
+            annT = ann_counts = None
+            if self.n_a and ann_ids is not None:
+                ann = torch.as_tensor(ann_ids).to(dev, torch.int64, non_blocking=True)
+                ann = ann.view(n_v, -1).contiguous()
+                A_pad, n_pad = max(16, _ceil(self.n_a, 16)), max(128, _ceil(n_s, 128))
+                annT = torch.empty(A_pad, n_pad, dtype=torch.int8, device=dev)
+                ann_counts = torch.empty(self.n_a, **i64)
+                call("atlas_ctx_annotations", ptr(sub_idx), ptr(counts), ptr(ann), n_v, ann.shape[1], self.n_a,
+                     ptr(annT), A_pad, n_pad, ptr(ann_counts), st.cuda_stream)
+            valid32 = vr.to(torch.int32)
+            ready = torch.cuda.Event()
+            ready.record(st)
+        return BatchCtx(T=T, valid_rows=vr, tok=tk, key=key, rowmap=rowmap32, sub_idx=sub_idx[:n_s],
+                        res_in_sub=res_in_sub[:n_r], n_v=n_v, n_s=n_s, n_r=n_r, sub_rows=sub_rows32[:n_s],
+                        rowmap32=rowmap32, valid32=valid32, sub_rows32=sub_rows32[:n_s], res_rows32=res_rows32[:n_r],
+                        res_vidx32=res_vidx32[:n_r], key_order32=key_order32, annT=annT, ann_counts=ann_counts,
+                        ready=ready)
+
     def _cap(self, ctx, l=None) -> int:
         f = self.cfg.cap_frac
         if self.cfg.cap_frac_early > 0 and l is not None and l < self.cfg.early_layers:
@@ -349,6 +404,12 @@ class Atlas:
         """Thresholds for this batch from the state at batch start (device only, no sync)."""
         if ctx.valid_rows.device != self.dev:
             ctx = ctx.to(self.dev)
+        if ctx.ready is not None:  # built on another stream (make_ctx_device): order and keep its memory
+            cur = torch.cuda.current_stream(self.dev)
+            cur.wait_event(ctx.ready)
+            for t in ctx.__dict__.values():
+                if torch.is_tensor(t) and t.is_cuda:
+                    t.record_stream(cur)
         if redo_layers is not None:
             if redo_layers:
                 raise ValueError("end_batch never requests a redo: overflowed layers take the dense path in the hook")

@@ -25,6 +25,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxB = 8;
 constexpr int kStage = 1024;  // staged records per CTA (top: <= 2K; reservoir: <= 2*B*Kr)
+constexpr int kDenseSmemMax = 227 * 1024;  // opt-in shared memory per CTA
 
 struct Lists {
   int32_t* g; int64_t* sc; int64_t* tok; float* val; int32_t* n; int64_t cap;
@@ -108,9 +109,11 @@ __device__ void flush(Staged& st, const Lists& o, int32_t* err, int* s_base) {
 }
 
 struct ColShared {
-  uint32_t hist[2][256];
+  uint32_t whist[kThreads / 32][2][256];  // per-warp digit histograms (no cross-warp atomics)
+  uint32_t hist[2][256];                  // their sum
   unsigned long long P[2];
   int need[2], nbits[2], done[2];
+  int cand[2];                            // admissible top-K candidates per pole
   int scan[kThreads / 32][2 * kMaxB];
   int base;
   Staged st;
@@ -118,24 +121,76 @@ struct ColShared {
 
 // One column d of the layer (the CTA's threads together): top-K radix select and reservoir runs.
 template <int DT>
-__device__ __forceinline__ void dense_column(ColShared& sh, int64_t d, const typename Elem<DT>::T* __restrict__ HT,
+__device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T* scol, int64_t d,
+                                             const typename Elem<DT>::T* __restrict__ HT,
                                              int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
                                              const int64_t* __restrict__ key, const int32_t* __restrict__ key_order,
                                              int64_t layer, int64_t D, int B, int64_t K, int64_t Kr, int reservoir,
                                              const float* __restrict__ top_seed, const int64_t* __restrict__ top_k,
                                              const int64_t* __restrict__ res_s, const int64_t* __restrict__ res_seed,
                                              const float* __restrict__ E, Lists top, Lists res, int32_t* __restrict__ err) {
-  const typename Elem<DT>::T* col = HT + d * ldh;
+  using T = typename Elem<DT>::T;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool select_all = n_v <= K;
+  const T* col = HT + d * ldh;
+  if (scol != nullptr) {  // the whole column in shared memory: every pass below reads it from there
+    const int64_t nvec = (ldh * (int64_t)sizeof(T)) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(col);
+    uint4* dst = reinterpret_cast<uint4*>(scol);
+    for (int64_t i = tid; i < nvec; i += kThreads) dst[i] = __ldcs(src + i);
+    col = scol;
+  }
+  int64_t kth[2];
+  float seed[2];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int64_t g = (layer * 2 + p) * D + d;
+    kth[p] = top_k[g * K + (K - 1)];
+    seed[p] = top_seed[g];
+  }
   if (tid < 2) {
     sh.P[tid] = 0;
     sh.need[tid] = (int)K;
     sh.nbits[tid] = 0;
-    sh.done[tid] = select_all ? 1 : 0;
+    sh.cand[tid] = 0;
   }
   if (tid == 0) sh.st.n = 0;
   __syncthreads();
+  // Admissible top-K candidates of the batch: s > seed and top_key(s, tok) above the state's K-th
+  // key (only those can enter the state). When a pole has at most K of them they are exactly the
+  // records to merge, and its radix select is skipped (the common case once the state is full).
+  {
+    int c0 = 0, c1 = 0;
+    const uint64_t ku0 = (uint64_t)kth[0] ^ 0x8000000000000000ull, ku1 = (uint64_t)kth[1] ^ 0x8000000000000000ull;
+    for (int64_t i = tid; i < n_v; i += kThreads) {
+      const float h = Elem<DT>::f(col[i]);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const float s = p ? -h : h;
+        if (!(s > seed[p])) continue;
+        const uint64_t ku = p ? ku1 : ku0;
+        const uint32_t hi = key_hi(s);
+        if (hi > (uint32_t)(ku >> 32)) {
+          (p ? c1 : c0)++;
+        } else if (hi == (uint32_t)(ku >> 32)) {
+          const uint64_t c = ((uint64_t)hi << 32) | (uint64_t)(kM32 - (uint32_t)tok[i]);
+          if (c > ku) (p ? c1 : c0)++;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, o);
+      c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, o);
+    }
+    if (lane == 0) {
+      atomicAdd(&sh.cand[0], c0);
+      atomicAdd(&sh.cand[1], c1);
+    }
+  }
+  __syncthreads();
+  if (tid < 2) sh.done[tid] = (n_v <= K || sh.cand[tid] <= K) ? 1 : 0;
+  __syncthreads();
+  const bool select_all = sh.done[0] && sh.done[1];
   // ------------------------------------------------------------------ top-K radix select
   if (!select_all) {
     for (int pass = 0; pass < 8; ++pass) {
@@ -152,7 +207,7 @@ __device__ __forceinline__ void dense_column(ColShared& sh, int64_t d, const typ
         __syncthreads();
         continue;
       }
-      for (int i = tid; i < 512; i += kThreads) (&sh.hist[0][0])[i] = 0;
+      for (int i = tid; i < (kThreads / 32) * 512; i += kThreads) (&sh.whist[0][0][0])[i] = 0;
       __syncthreads();
       const int shift = 56 - 8 * pass;
       const bool act0 = !sh.done[0], act1 = !sh.done[1];
@@ -169,12 +224,19 @@ __device__ __forceinline__ void dense_column(ColShared& sh, int64_t d, const typ
           const unsigned long long P = p == 0 ? P0 : P1;
           const uint64_t hi = (uint64_t)key_hi(p ? -h : h);
           if (pass < 4) {
-            if (nb == 0 || (hi >> (32 - nb)) == P) atomicAdd(&sh.hist[p][(hi >> (24 - 8 * pass)) & 0xFF], 1u);
+            if (nb == 0 || (hi >> (32 - nb)) == P) atomicAdd(&sh.whist[warp][p][(hi >> (24 - 8 * pass)) & 0xFF], 1u);
           } else if (hi == (P >> (nb - 32))) {
             const uint64_t c = (hi << 32) | (uint64_t)(kM32 - (uint32_t)tok[i]);
-            if ((c >> (64 - nb)) == P) atomicAdd(&sh.hist[p][(c >> shift) & 0xFF], 1u);
+            if ((c >> (64 - nb)) == P) atomicAdd(&sh.whist[warp][p][(c >> shift) & 0xFF], 1u);
           }
         }
+      }
+      __syncthreads();
+      for (int i = tid; i < 512; i += kThreads) {
+        uint32_t t = 0;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) t += (&sh.whist[w][0][0])[i];
+        (&sh.hist[0][0])[i] = t;
       }
       __syncthreads();
       if (warp < 2 && !sh.done[warp]) {
@@ -218,15 +280,7 @@ __device__ __forceinline__ void dense_column(ColShared& sh, int64_t d, const typ
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const int nb = sh.nbits[p];
-    thr[p] = select_all ? 0ull : (nb >= 64 ? sh.P[p] : (nb == 0 ? 0ull : (sh.P[p] << (64 - nb))));
-  }
-  int64_t kth[2];
-  float seed[2];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const int64_t g = (layer * 2 + p) * D + d;
-    kth[p] = top_k[g * K + (K - 1)];
-    seed[p] = top_seed[g];
+    thr[p] = (nb >= 64 ? sh.P[p] : (nb == 0 ? 0ull : (sh.P[p] << (64 - nb))));
   }
   for (int64_t i = tid; i < n_v; i += kThreads) {
     const float h = Elem<DT>::f(col[i]);
@@ -352,14 +406,17 @@ dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, in
                     int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
                     const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
                     const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
-                    int64_t cap, int force, Lists top, Lists res, int32_t* __restrict__ err) {
+                    int64_t cap, int force, Lists top, Lists res, int32_t* __restrict__ err, int col_in_smem) {
   if (!triggered(count, cap, force)) return;
   extern __shared__ __align__(16) unsigned char col_raw[];
   ColShared& sh = *reinterpret_cast<ColShared*>(col_raw);
+  // with col_in_smem the column (ldh elements) is staged after the shared state
+  auto* scol = col_in_smem ? reinterpret_cast<typename Elem<DT>::T*>(col_raw + ((sizeof(ColShared) + 15) / 16) * 16)
+                           : nullptr;
   for (int64_t d = blockIdx.x; d < D; d += gridDim.x) {
-    dense_column<DT>(sh, d, HT, ldh, n_v, tok, key, key_order, layer, D, B, K, Kr, reservoir, top_seed, top_k, res_s,
-                     res_seed, E, top, res, err);
-    __syncthreads();  // the next column re-initialises the shared state
+    dense_column<DT>(sh, scol, d, HT, ldh, n_v, tok, key, key_order, layer, D, B, K, Kr, reservoir, top_seed, top_k,
+                     res_s, res_seed, E, top, res, err);
+    __syncthreads();  // the next column re-initialises the shared state and the staged column
   }
 }
 
@@ -377,18 +434,23 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   dense_gather_kernel<T><<<g1, dim3(32, 8), 0, st>>>(reinterpret_cast<const T*>(H), D, ld, valid_rows, n_v, n8, HT, n8,
                                                      count, cap, force);
   if (int e = check_launch("atlas_dense_select: gather")) return e;
-  const size_t smem = sizeof(ColShared);
-  if (cudaFuncSetAttribute(dense_column_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  // the column goes to shared memory when it fits next to the shared state (C4: ~62 KB of bf16 per
+  // column, two CTAs per SM); otherwise it is read from the transposed copy in global memory
+  const size_t base_smem = ((sizeof(ColShared) + 15) / 16) * 16;
+  const size_t col_bytes = (size_t)n8 * sizeof(T);
+  const int col_in_smem = base_smem + col_bytes <= (size_t)kDenseSmemMax ? 1 : 0;
+  const size_t smem = col_in_smem ? base_smem + col_bytes : sizeof(ColShared);
+  if (cudaFuncSetAttribute(dense_column_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDenseSmemMax) !=
+      cudaSuccess)
     return fail(ATLAS_ERR_CUDA, "dense_select: cannot reserve %zu bytes of shared memory", smem);
-  static int per_sm = 0;  // resident CTAs per SM (registers bound it), queried once per instantiation
-  if (per_sm == 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_column_kernel<DT>, kThreads, smem) !=
-                          cudaSuccess ||
-                      per_sm < 1))
+  int per_sm = 0;  // resident CTAs per SM at this shared-memory size
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_column_kernel<DT>, kThreads, smem) != cudaSuccess ||
+      per_sm < 1)
     per_sm = 1;
   const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
   dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, key, key_order, layer, D, (int)B, K, Kr,
                                                                 reservoir, top_seed, top_k, res_s, res_seed, E, count,
-                                                                cap, force, top, res, err);
+                                                                cap, force, top, res, err, col_in_smem);
   return check_launch("atlas_dense_select: column");
 }
 

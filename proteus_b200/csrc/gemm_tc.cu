@@ -593,23 +593,25 @@ int launch_i8(const int8_t* masks, int64_t M, int64_t n_pad, const int8_t* annT,
 // bin counts of atlas_sub_stats AND the enrichment contingencies of atlas_count_gemm_i8, without
 // the int8 masks ever reaching HBM. A CTA owns 128 columns d (the M rows of every mask plane) and a
 // range of 128-row slabs of the subsample:
-//   16 producer warps: 4 threads per column, 32 rows each per slab. Each thread compares its rows
-//     against the column's edges as packed bf16 pairs (exact for bf16 inputs, as atlas_sub_stats),
-//     counts by popcount, sums in fp32 per 8 rows and fp64 across, and writes the 0/1 bytes of every
-//     (pole, level) plane straight into the UMMA K-major 128-byte-swizzled shared-memory tile
-//     (row d, byte i: 16-byte chunk (i / 16) ^ (d % 8)); the annotation one-hots of the slab are
-//     copied into the same layout. A proxy fence and a named barrier later, one thread arrives on
-//     the stage's mbarrier.
-//   1 MMA warp: per slab and plane, four tcgen05.mma kind::i8 (M=128, N=A_pad, K=32) into its own
-//     TMEM accumulator (int32, exact), then a commit that frees the stage.
+//   16 producer warps: 4 threads per column, 32 rows each per slab, loaded one slab ahead. Each
+//     thread compares its rows against the column's edges as packed bf16 pairs (exact for bf16
+//     inputs, as atlas_sub_stats), counts by popcount, sums in fp32 per 8 rows and fp64 across, and
+//     writes the 0/1 bytes of every (pole, level) plane straight into the UMMA K-major
+//     128-byte-swizzled shared-memory tile (row d, byte i: 16-byte chunk (i / 16) ^ (d % 8)); the
+//     annotation one-hots of the slab are copied into the same layout. After a proxy fence each
+//     warp arrives on the stage's mbarrier (16 arrivals complete it); warps run ahead of each other
+//     up to the two stages.
+//   the last producer warp also issues the MMAs: once a stage is full, per plane four tcgen05.mma
+//     kind::i8 (M=128, N=A_pad, K=32) into its own TMEM accumulator (int32, exact), then a commit
+//     that frees the stage (16 warps, 128 registers per thread).
 //   epilogue: warps 0-3 read the accumulators (lane = column) and add them into enr (int64).
 // Column sums of a CTA range are fp64 partials; with several ranges per column the last CTA to
 // finish (ticket counter) adds the partials in range order, so the result does not depend on CTA
 // timing. Bin counts and contingencies are integers added atomically.
 constexpr int SE_M = 128;
 constexpr int SE_K = 128;
-constexpr int SE_PW = 16;
-constexpr int SE_THREADS = (SE_PW + 1) * 32;
+constexpr int SE_PW = 16;                // producer warps; the last one also issues the MMAs
+constexpr int SE_THREADS = SE_PW * 32;
 constexpr int SE_STAGES = 2;
 constexpr int SE_PLANES = 6;
 constexpr int SE_MAXB = 8;
@@ -636,13 +638,32 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Packed bf16 compares of two register words: 0xFFFF in each half where the compare holds
+// (ordered: false for NaN), the semantics of __hge2_mask / __hle2_mask without a round trip of
+// the operands through memory.
+__device__ __forceinline__ uint32_t bf2_ge_mask(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_le_mask(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("set.le.u32.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float v) {
+  const uint32_t h = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+  return h | (h << 16);
+}
+
 // 0/1 bytes of 8 rows from the four 32-bit compare masks (0xFFFF per true half) of a vector
 __device__ __forceinline__ uint64_t mask_bytes(const uint32_t (&m)[4]) {
   return (uint64_t)(__byte_perm(m[0], m[1], 0x6420) & 0x01010101u) |
          ((uint64_t)(__byte_perm(m[2], m[3], 0x6420) & 0x01010101u) << 32);
 }
 
-template <int AP>
+template <int AP, int NB>
 __global__ void __launch_bounds__(SE_THREADS, 1)
 stats_enrich_kernel(const __nv_bfloat16* __restrict__ XT, int64_t ldx, int64_t col0, int64_t n, int64_t D,
                     const float* __restrict__ E0, const float* __restrict__ E1, int B, SELevels lev, int NL,
@@ -660,162 +681,180 @@ stats_enrich_kernel(const __nv_bfloat16* __restrict__ XT, int64_t ldx, int64_t c
   const int planes = 2 * NL;
   if (threadIdx.x == 0) {
     for (int i = 0; i < SE_STAGES; ++i) {
-      mbar_init(&s.full[i], 1);
+      mbar_init(&s.full[i], SE_PW);  // one arrival per producer warp
       mbar_init(&s.empty[i], 1);
     }
     mbar_init(&s.tfull, 1);
     s.abort = 0;
     fence_barrier_init();
   }
-  if (warp == SE_PW) tmem_alloc(&s.tmem_base, tcols);
+  constexpr int kMmaWarp = SE_PW - 1;
+  if (warp == kMmaWarp) tmem_alloc(&s.tmem_base, tcols);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
-  if (warp == SE_PW) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_s8_s32(SE_M, AP);
-      for (int k = 0; k < nk; ++k) {
-        const int st = k % SE_STAGES;
-        const uint32_t ph = (k / SE_STAGES) & 1;
-        if (!mbar_wait(&s.full[st], ph, 211)) break;
-        tc_fence_after();
-        const uint32_t b_addr = smem_u32(s.b[st]);
-        for (int pl = 0; pl < planes; ++pl) {
-          const uint32_t a_addr = smem_u32(s.a[st][pl]);
-#pragma unroll
-          for (int kk = 0; kk < SE_K / 32; ++kk)
-            mma_i8(tmem + (uint32_t)(pl * AP), sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
-                   (k == 0 && kk == 0) ? 0u : 1u);
-        }
-        mma_commit(&s.empty[st]);
-      }
-      mma_commit(&s.tfull);
-    }
-  } else {
+  {
     // ---------------------------------------------------------------- producers
     const int t = threadIdx.x;
     const int r = t >> 2, prt = t & 3;
     const int64_t d = d0 + r;
     const bool dok = d < D;
-    __nv_bfloat162 pe[SE_MAXB], ne[SE_MAXB];
-    int levof[SE_MAXB];  // bit j: level j sits on edge b
+    uint32_t pe[NB], ne[NB];  // edges as packed bf16 pairs
+    uint32_t levbits = 0;     // bits 3b..3b+2: the levels j sitting on edge b
 #pragma unroll
-    for (int b = 0; b < SE_MAXB; ++b) {
-      const bool ok = dok && b < B;
-      pe[b] = __bfloat162bfloat162(__float2bfloat16_ru(ok ? E0[d * B + b] : __int_as_float(0x7F800000)));
-      ne[b] = __bfloat162bfloat162(__float2bfloat16_rd(ok ? -E1[d * B + b] : __int_as_float(0xFF800000)));
-      int lm = 0;
+    for (int b = 0; b < NB; ++b) {
+      const bool ok = dok;
+      const uint32_t hp = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_ru(ok ? E0[d * B + b] : __int_as_float(0x7F800000)));
+      const uint32_t hn = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rd(ok ? -E1[d * B + b] : __int_as_float(0xFF800000)));
+      pe[b] = hp | (hp << 16);
+      ne[b] = hn | (hn << 16);
 #pragma unroll
       for (int j = 0; j < 3; ++j)
-        if (j < NL && lev.v[j] == b) lm |= 1 << j;
-      levof[b] = lm;
+        if (j < NL && lev.v[j] == b) levbits |= 1u << (3 * b + j);
     }
-    int c0[SE_MAXB], c1[SE_MAXB];
+    int c0[NB], c1[NB];
 #pragma unroll
-    for (int b = 0; b < SE_MAXB; ++b) c0[b] = c1[b] = 0;
+    for (int b = 0; b < NB; ++b) c0[b] = c1[b] = 0;
     double acc_s = 0.0, acc_q = 0.0;
     const __nv_bfloat16* col = XT + (dok ? d : 0) * ldx + col0;
+    // the slab's 4 chunks of this thread (and, for t < AP*8, one 16-byte chunk of the one-hots),
+    // loaded one slab ahead of their use so the global-load latency overlaps the compares
+#define SE_LOAD_SLAB(KK, RAW0, RAW1, RAW2, RAW3, ANN)                                                        \
+  {                                                                                                         \
+    const int64_t row0_ = (int64_t)(k_begin + (KK)) * SE_K;                                                 \
+    const int64_t i0_ = row0_ + prt * 8;                                                                    \
+    RAW0 = (dok && i0_ < n) ? __ldcs(reinterpret_cast<const uint4*>(col + i0_)) : make_uint4(0u, 0u, 0u, 0u);  \
+    RAW1 = (dok && i0_ + 32 < n) ? __ldcs(reinterpret_cast<const uint4*>(col + i0_ + 32)) : make_uint4(0u, 0u, 0u, 0u); \
+    RAW2 = (dok && i0_ + 64 < n) ? __ldcs(reinterpret_cast<const uint4*>(col + i0_ + 64)) : make_uint4(0u, 0u, 0u, 0u); \
+    RAW3 = (dok && i0_ + 96 < n) ? __ldcs(reinterpret_cast<const uint4*>(col + i0_ + 96)) : make_uint4(0u, 0u, 0u, 0u); \
+    if (t < AP * 8) ANN = *reinterpret_cast<const uint4*>(annT + (int64_t)(t >> 3) * n_pad + row0_ + (t & 7) * 16); \
+  }
+    uint4 c0v, c1v, c2v, c3v, n0v, n1v, n2v, n3v;
+    uint4 cur_ann = make_uint4(0u, 0u, 0u, 0u), nxt_ann = cur_ann;
+    c0v = c1v = c2v = c3v = n0v = n1v = n2v = n3v = cur_ann;
+    if (nk > 0) SE_LOAD_SLAB(0, c0v, c1v, c2v, c3v, cur_ann)
     bool ok_run = true;
-    // every producer takes the same nk barrier steps: after a failed wait the shared abort flag
-    // (read after each barrier) turns the remaining steps into no-ops for all of them
-    for (int k = 0; k < nk; ++k) {
+    for (int k = 0; k < nk && ok_run; ++k) {
       const int st = k % SE_STAGES;
       const uint32_t ph = (k / SE_STAGES) & 1;
-      if (ok_run && k >= SE_STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 212)) {
+      if (*reinterpret_cast<volatile int*>(&s.abort)) {
         ok_run = false;
-        s.abort = 1;
+        break;
       }
-      if (ok_run) {
-        const int64_t slab_row0 = (int64_t)(k_begin + k) * SE_K;
+      if (k + 1 < nk) SE_LOAD_SLAB(k + 1, n0v, n1v, n2v, n3v, nxt_ann)
+      if (k >= SE_STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 212)) {
+        s.abort = 1;  // the other warps see it before their next slab
+        ok_run = false;
+        break;
+      }
+      const int64_t slab_row0 = (int64_t)(k_begin + k) * SE_K;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int c = q * 4 + prt;  // 8-row chunk of the slab
-          const int64_t i = slab_row0 + c * 8;
-          uint32_t w4[4] = {0u, 0u, 0u, 0u};
-          uint32_t vm[4] = {0u, 0u, 0u, 0u};
-          if (dok && i < n) {
-            const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(col + i));
-            w4[0] = raw.x; w4[1] = raw.y; w4[2] = raw.z; w4[3] = raw.w;
+      for (int q = 0; q < 4; ++q) {
+        const int c = q * 4 + prt;  // 8-row chunk of the slab
+        const int64_t i = slab_row0 + c * 8;
+        const uint4 cq = q == 0 ? c0v : (q == 1 ? c1v : (q == 2 ? c2v : c3v));
+        uint32_t w4[4] = {cq.x, cq.y, cq.z, cq.w};
+        const bool full = dok && i + 8 <= n;
+        uint32_t vm[4] = {0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu};
+        if (!full) {  // the ragged end of the subsample (or a column past D): rows >= n neither count nor match
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              const int64_t rr = i + 2 * w;
-              vm[w] = (rr < n ? 0x0000FFFFu : 0u) | (rr + 1 < n ? 0xFFFF0000u : 0u);
-              w4[w] &= vm[w];
-            }
-            float s32 = 0.0f, q32 = 0.0f;
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              const float lo = __uint_as_float(w4[w] << 16), hi = __uint_as_float(w4[w] & 0xFFFF0000u);
-              s32 += lo;
-              s32 += hi;
-              q32 = fmaf(lo, lo, q32);
-              q32 = fmaf(hi, hi, q32);
-            }
-            acc_s += (double)s32;
-            acc_q += (double)q32;
-          }
-          uint64_t wp[3] = {0, 0, 0}, wn[3] = {0, 0, 0};
-#pragma unroll
-          for (int b = 0; b < SE_MAXB; ++b) {
-            if (b >= B) break;
-            uint32_t mp[4], mn[4];
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[w]);
-              mp[w] = __hge2_mask(h2, pe[b]) & vm[w];
-              mn[w] = __hle2_mask(h2, ne[b]) & vm[w];
-            }
-            c0[b] += __popc(mp[0]) + __popc(mp[1]) + __popc(mp[2]) + __popc(mp[3]);
-            c1[b] += __popc(mn[0]) + __popc(mn[1]) + __popc(mn[2]) + __popc(mn[3]);
-            const int lm = levof[b];
-            if (lm) {
-              const uint64_t bp = mask_bytes(mp), bn = mask_bytes(mn);
-#pragma unroll
-              for (int j = 0; j < 3; ++j)
-                if (lm & (1 << j)) {
-                  wp[j] = bp;
-                  wn[j] = bn;
-                }
-            }
-          }
-          const uint32_t off = (uint32_t)r * 128u + ((uint32_t)((c >> 1) ^ (r & 7)) << 4) + ((uint32_t)(c & 1) << 3);
-#pragma unroll
-          for (int j = 0; j < 3; ++j) {
-            if (j < NL) {
-              *reinterpret_cast<uint64_t*>(s.a[st][j] + off) = wp[j];
-              *reinterpret_cast<uint64_t*>(s.a[st][NL + j] + off) = wn[j];
-            }
+          for (int w = 0; w < 4; ++w) {
+            const int64_t rr = i + 2 * w;
+            vm[w] = dok ? ((rr < n ? 0x0000FFFFu : 0u) | (rr + 1 < n ? 0xFFFF0000u : 0u)) : 0u;
+            w4[w] &= vm[w];
           }
         }
-        if (t < AP * 8) {  // the slab's annotation one-hots: row a, 16-byte chunk c16
-          const int a_row = t >> 3, c16 = t & 7;
-          const uint4 v = *reinterpret_cast<const uint4*>(annT + (int64_t)a_row * n_pad + slab_row0 + c16 * 16);
-          *reinterpret_cast<uint4*>(s.b[st] + a_row * 128 + ((c16 ^ (a_row & 7)) << 4)) = v;
+        {
+          float s32 = 0.0f, q32 = 0.0f;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const float lo = __uint_as_float(w4[w] << 16), hi = __uint_as_float(w4[w] & 0xFFFF0000u);
+            s32 += lo;
+            s32 += hi;
+            q32 = fmaf(lo, lo, q32);
+            q32 = fmaf(hi, hi, q32);
+          }
+          acc_s += (double)s32;
+          acc_q += (double)q32;
         }
-        fence_proxy_async_smem();
+        const uint32_t off = (uint32_t)r * 128u + ((uint32_t)((c >> 1) ^ (r & 7)) << 4) + ((uint32_t)(c & 1) << 3);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          uint32_t mp[4], mn[4];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            mp[w] = bf2_ge_mask(w4[w], pe[b]);
+            mn[w] = bf2_le_mask(w4[w], ne[b]);
+            if (!full) {
+              mp[w] &= vm[w];
+              mn[w] &= vm[w];
+            }
+          }
+          c0[b] += __popc(mp[0]) + __popc(mp[1]) + __popc(mp[2]) + __popc(mp[3]);
+          c1[b] += __popc(mn[0]) + __popc(mn[1]) + __popc(mn[2]) + __popc(mn[3]);
+          const uint32_t lm = (levbits >> (3 * b)) & 7u;
+          if (lm) {  // this edge is an enrichment level: its 0/1 bytes go straight to the plane tiles
+            const uint64_t bp = mask_bytes(mp), bn = mask_bytes(mn);
+#pragma unroll
+            for (int j = 0; j < 3; ++j)
+              if (lm & (1u << j)) {
+                *reinterpret_cast<uint64_t*>(s.a[st][j] + off) = bp;
+                *reinterpret_cast<uint64_t*>(s.a[st][NL + j] + off) = bn;
+              }
+          }
+        }
       }
-      named_sync_producers();
-      ok_run = ok_run && !*reinterpret_cast<volatile int*>(&s.abort);
-      if (t == 0 && ok_run) mbar_arrive(&s.full[st]);
+      if (t < AP * 8) {  // the slab's annotation one-hots: row a, 16-byte chunk c16
+        const int a_row = t >> 3, c16 = t & 7;
+        *reinterpret_cast<uint4*>(s.b[st] + a_row * 128 + ((c16 ^ (a_row & 7)) << 4)) = cur_ann;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.full[st]);  // one arrival per producer warp
+      if (warp == kMmaWarp) {  // once every warp has filled the stage: its MMAs, then a commit that frees it
+        if (lane == 0) {
+          if (mbar_wait(&s.full[st], ph, 211)) {
+            tc_fence_after();
+            constexpr uint32_t idesc = idesc_s8_s32(SE_M, AP);
+            const uint32_t b_addr = smem_u32(s.b[st]);
+            for (int pl = 0; pl < planes; ++pl) {
+              const uint32_t a_addr = smem_u32(s.a[st][pl]);
+#pragma unroll
+              for (int kk = 0; kk < SE_K / 32; ++kk)
+                mma_i8(tmem + (uint32_t)(pl * AP), sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32),
+                       idesc, (k == 0 && kk == 0) ? 0u : 1u);
+            }
+            mma_commit(&s.empty[st]);
+          } else {
+            s.abort = 1;
+          }
+        }
+        __syncwarp();
+      }
+      c0v = n0v;
+      c1v = n1v;
+      c2v = n2v;
+      c3v = n3v;
+      cur_ann = nxt_ann;
     }
+#undef SE_LOAD_SLAB
+    if (warp == kMmaWarp && lane == 0) mma_commit(&s.tfull);  // completes when every MMA above has
     // ---------------------------------------------------------------- column statistics
 #pragma unroll
     for (int o = 1; o <= 2; o <<= 1) {
       acc_s += __shfl_xor_sync(0xFFFFFFFFu, acc_s, o);
       acc_q += __shfl_xor_sync(0xFFFFFFFFu, acc_q, o);
 #pragma unroll
-      for (int b = 0; b < SE_MAXB; ++b) {
+      for (int b = 0; b < NB; ++b) {
         c0[b] += __shfl_xor_sync(0xFFFFFFFFu, c0[b], o);
         c1[b] += __shfl_xor_sync(0xFFFFFFFFu, c1[b], o);
       }
     }
     if (prt == 0 && dok) {
 #pragma unroll
-      for (int b = 0; b < SE_MAXB; ++b) {
-        if (b >= B) break;
-        const int nx0 = (b + 1 < B) ? c0[b + 1] : 0;
-        const int nx1 = (b + 1 < B) ? c1[b + 1] : 0;
+      for (int b = 0; b < NB; ++b) {
+        const int nx0 = (b + 1 < NB) ? c0[b + 1] : 0;
+        const int nx1 = (b + 1 < NB) ? c1[b + 1] : 0;
         const unsigned long long v0 = (unsigned long long)((c0[b] - nx0) >> 4);  // 16 mask bits per row
         const unsigned long long v1 = (unsigned long long)((c1[b] - nx1) >> 4);
         if (v0) atomicAdd(bins + d * B + b, v0);
@@ -878,14 +917,14 @@ stats_enrich_kernel(const __nv_bfloat16* __restrict__ XT, int64_t ldx, int64_t c
     }
   }
   __syncthreads();
-  if (warp == SE_PW) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, tcols);
   }
 }
 
-template <int AP>
-int launch_stats_enrich(const __nv_bfloat16* XT, int64_t ldx, int64_t col0, int64_t n, int64_t D, const float* E0,
+template <int AP, int NB>
+int launch_stats_enrich_b(const __nv_bfloat16* XT, int64_t ldx, int64_t col0, int64_t n, int64_t D, const float* E0,
                         const float* E1, int B, const SELevels& lev, int NL, const int8_t* annT, int64_t n_pad, int A,
                         double* sum, double* sq, int64_t* bins, int64_t* enr, void* ws, cudaStream_t st) {
   const int n_slabs = (int)((n + SE_K - 1) / SE_K);
@@ -898,15 +937,29 @@ int launch_stats_enrich(const __nv_bfloat16* XT, int64_t ldx, int64_t col0, int6
   unsigned int* tickets = reinterpret_cast<unsigned int*>(ws);
   double* part = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(ws) + ((dtiles * 4 + 255) / 256) * 256);
   const size_t smem = sizeof(SESmem<AP>) + 1024;
-  if (cudaFuncSetAttribute(stats_enrich_kernel<AP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (cudaFuncSetAttribute(stats_enrich_kernel<AP, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return fail(ATLAS_ERR_CUDA, "sub_stats_enrich: cannot reserve %zu bytes of shared memory", smem);
   uint32_t tcols = 32;
   while (tcols < (uint32_t)(2 * NL * AP)) tcols <<= 1;
-  stats_enrich_kernel<AP><<<dim3((unsigned)dtiles, (unsigned)ks), SE_THREADS, smem, st>>>(
+  stats_enrich_kernel<AP, NB><<<dim3((unsigned)dtiles, (unsigned)ks), SE_THREADS, smem, st>>>(
       XT, ldx, col0, n, D, E0, E1, B, lev, NL, annT, n_pad, A, sum, sq, reinterpret_cast<unsigned long long*>(bins),
       reinterpret_cast<unsigned long long*>(enr), part, tickets, spp, n_slabs, tcols);
   return check_launch("atlas_sub_stats_enrich");
+}
+
+template <int AP>
+int launch_stats_enrich(const __nv_bfloat16* XT, int64_t ldx, int64_t col0, int64_t n, int64_t D, const float* E0,
+                        const float* E1, int B, const SELevels& lev, int NL, const int8_t* annT, int64_t n_pad, int A,
+                        double* sum, double* sq, int64_t* bins, int64_t* enr, void* ws, cudaStream_t st) {
+  switch (B) {
+#define ATLAS_SE_B(NBV) \
+  case NBV:             \
+    return launch_stats_enrich_b<AP, NBV>(XT, ldx, col0, n, D, E0, E1, B, lev, NL, annT, n_pad, A, sum, sq, bins, enr, ws, st);
+    ATLAS_SE_B(1) ATLAS_SE_B(2) ATLAS_SE_B(3) ATLAS_SE_B(4) ATLAS_SE_B(5) ATLAS_SE_B(6) ATLAS_SE_B(7) ATLAS_SE_B(8)
+#undef ATLAS_SE_B
+    default: return fail(ATLAS_ERR_ARG, "sub_stats_enrich: B must be 1..%d", SE_MAXB);
+  }
 }
 
 }  // namespace

@@ -149,8 +149,34 @@ def warm_up(group=None, device=None):
         torch.cuda.synchronize(dev)
 
 
+class _Sections:
+    """CUDA-event (or, on CPU, wall-clock) times of the combine's sections, in ms."""
+
+    def __init__(self, out: dict | None, device):
+        self.out, self.cuda = out, out is not None and device.type == "cuda"
+        self.t = None
+
+    def mark(self, name: str | None):
+        if self.out is None:
+            return
+        if self.cuda:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+        else:
+            import time
+            e = time.perf_counter()
+        if self.t is not None:
+            prev_name, prev = self.t
+            if self.cuda:
+                e.synchronize()
+                self.out[prev_name] = prev.elapsed_time(e)
+            else:
+                self.out[prev_name] = (e - prev) * 1e3
+        self.t = (name, e) if name is not None else None
+
+
 @torch.no_grad()
-def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
+def merge_states(atlas, group=None, row_merge=None, gram: bool = True, timings: dict | None = None):
     """Combine the shard atlases of all ranks in place; afterwards every rank holds the merged
     atlas (equal to merge_from applied over all shards). `atlas` needs the reference's state
     attributes (top_k/top_t/top_s, res_s/res_t/res_v, sub_*, enr/ann_tot, n_seen/n_sub, stats,
@@ -159,15 +185,19 @@ def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
     if world == 1:
         return atlas
     row_merge = row_merge or _row_merge_cuda
+    sec = _Sections(timings, atlas.top_k.device)
+    sec.mark("signature_ms")
     # the shards must share edges, config and both seeds (atlas/core.py:632-634)
     sigs = [None] * world
     dist.all_gather_object(sigs, shard_signature(atlas), group=group)
     if len(set(sigs)) != 1:
         raise ValueError("shards must share edges, config and seeds (derive them from the GLOBAL stream)")
+    sec.mark("rows_ms")
     atlas.top_k, atlas.top_t, atlas.top_s = _exchange_rows(atlas.top_k, atlas.top_t, atlas.top_s, (-1, float("-inf")),
                                                            world, group, row_merge)
     atlas.res_s, atlas.res_t, atlas.res_v = _exchange_rows(atlas.res_s, atlas.res_t, atlas.res_v, (-1, float("nan")),
                                                            world, group, row_merge)
+    sec.mark("sums_ms")
     for k in ("sub_bin",) + (("enr", "ann_tot") if getattr(atlas, "n_a", 0) else ()):
         t = getattr(atlas, k)
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
@@ -177,12 +207,14 @@ def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
     cnt = torch.tensor([atlas.n_seen, atlas.n_sub, getattr(atlas, "gram_rows", 0)], dtype=torch.int64, device=dev)
     dist.all_reduce(cnt, op=dist.ReduceOp.SUM, group=group)
     atlas.n_seen, atlas.n_sub = int(cnt[0]), int(cnt[1])
+    sec.mark("gram_ms")
     if gram and getattr(atlas, "gram", None) is not None:
         atlas.flush_gram()
         for l in range(atlas.gram64.shape[0]):
             g = atlas.gram64[l].to(dev)
             atlas.gram64[l].copy_(_reduce_slices_in_rank_order(g, world, group).to(atlas.gram64.device))
         atlas.gram_rows = int(cnt[2])
+    sec.mark("stats_ms")
     stats = [None] * world
     dist.all_gather_object(stats, dict(atlas.stats), group=group)
     merged = {}
@@ -190,4 +222,5 @@ def merge_states(atlas, group=None, row_merge=None, gram: bool = True):
         for k, v in st.items():
             merged[k] = merged.get(k, 0) + v
     atlas.stats = merged
+    sec.mark(None)
     return atlas

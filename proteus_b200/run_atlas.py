@@ -189,6 +189,31 @@ def _dataset(spec: str):
     return SwissProt(spec)
 
 
+def overhead_summary(paired: list) -> dict:
+    """Atlas overhead vs the hook-free forward of the same batch (atlas pass / forward - 1) over the
+    paired batches, as the reference reports it (results/README.md:205-208): whole run, the prefix
+    (batches 0-59), the steady state (the last 1,600 paired batches, or the last half of a shorter
+    run) and windows of the plan, each as median / mean. `paired`: (global batch index, overhead)."""
+    import statistics
+    if not paired:
+        return {"paired_batches": 0}
+    paired = sorted(paired)
+
+    def mm(xs):
+        xs = [x for _, x in xs]
+        return {"n": len(xs), "median": statistics.median(xs), "mean": statistics.fmean(xs)} if xs else None
+
+    n = len(paired)
+    steady = paired[-1600:] if n >= 3200 else paired[n // 2:]
+    out = {"paired_batches": n, "whole": mm(paired), "prefix_0_59": mm([x for x in paired if x[0] < 60]),
+           "steady": mm(steady), "steady_from_batch": steady[0][0]}
+    last = paired[-1][0] + 1
+    edges = [0, 100, 1000, 3000, max(3000, last)]
+    out["windows"] = {f"{a}-{b}": mm([x for x in paired if a <= x[0] < b]) for a, b in zip(edges[:-1], edges[1:])
+                      if any(a <= x[0] < b for x in paired)}
+    return out
+
+
 class Prefetch:
     """Items of `it` produced `n` ahead on a background thread (the batch and its host-side context,
     as the reference's prefetch thread builds them). `close()` stops the producer and joins it: the
@@ -368,6 +393,7 @@ def main(argv=None):
 
     t2 = time.time()
     n_done = 0
+    paired = []  # (global batch index, atlas overhead vs the paired hook-free forward)
     # with several ranks every stop is collective (Lockstep): a rank that reaches its deadline or
     # cap stops all ranks at the same step, and ranks whose shard is exhausted wait for the others,
     # so no rank enters the combine's collectives while another still streams or has returned
@@ -427,6 +453,8 @@ def main(argv=None):
                        "t_end": time.time(), "fwd_only_s": fwd_s, "atlas_pass_s": atlas_s,
                        "overhead_vs_fwd": (atlas_s / fwd_s - 1) if fwd_s else None, "gram_flushed": gram_flushed,
                        "flops": flops_per_batch(info, b.n_rows, b.input_ids.shape[1]), "redo_layers": []}
+                if fwd_s:
+                    paired.append((bi * world + rank, atlas_s / fwd_s - 1))
                 n_done += 1
                 bi += 1
                 last_ckpt_s = None
@@ -478,9 +506,19 @@ def main(argv=None):
     writer.wait()
     logf.close()
     atlas.check_errors()
+    combine_s = None
     if world > 1:
-        from .dist import merge_states
+        from .dist import merge_states, warm_up
+        parts = [None] * world
+        torch.distributed.all_gather_object(parts, paired)
+        paired = [x for part in parts for x in part]
+        warm_up(device=torch.device(dev))
+        sync(dev)
+        tc0 = time.time()
         merge_states(atlas)
+        sync(dev)
+        combine_s = time.time() - tc0
+        log(f"[atlas] shard states of {world} ranks combined in {combine_s:.2f}s")
     if rank != 0:
         torch.distributed.destroy_process_group()
         return
@@ -494,7 +532,9 @@ def main(argv=None):
                for k in ("top_val", "top_tok", "res_tok", "res_val", "res_key", "sub_bin", "enr", "ann_tot", "edges")
                if k in res}
     sm = summary(True, len(plan))
-    sm.update({"digests": digests, "final_save_s": final_s, "gram_rows": res.get("gram_rows"),
+    sm.update({"overhead": overhead_summary(paired), "combine_s": combine_s,
+               "dense_layer_batches": res["stats"].get("dense_layer_batches"),
+               "digests": digests, "final_save_s": final_s, "gram_rows": res.get("gram_rows"),
                "res_seeded_bins": res["res_seeded_bins"], "res_seed_limited_bins": res["res_seed_limited_bins"],
                "top_seed_short_groups": res["top_seed_short_groups"]})
     (out / "run.json").write_text(json.dumps(sm, indent=1))

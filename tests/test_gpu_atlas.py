@@ -161,3 +161,50 @@ def test_kernel_api_dropins_run():
     assert v.dtype == torch.float32 and r.dtype == torch.int64 and c.dtype == torch.int64 and cnt.dim() == 0
     s, sq, cn, M = KN.sub_stats(H, torch.zeros(64, 5, device=DEV), torch.zeros(64, 5, device=DEV), (2, 3, 4))
     assert s.dtype == torch.float64 and cn.dtype == torch.int32 and M.shape == (2, 3, 64, 104)
+
+
+def test_make_ctx_device_equals_host_make_ctx():
+    """atlas_ctx_rows / atlas_ctx_annotations give every field of the host make_ctx (core.py:210-237):
+    keys, row map, subsample and bulk rows in order, key order, transposed one-hots and their totals,
+    on batches with padding rows, repeated and missing (-1) annotation ids, and an empty subsample."""
+    from proteus_b200.core import Atlas, AtlasConfig
+    rng = np.random.default_rng(5)
+    at = Atlas(1, 64, torch.zeros(1, 2, 64, 5), AtlasConfig(K=8, Kr=4, rho_res=0.05, rho_sub=0.2, seed=9), n_annot=11,
+               device=DEV)
+    side = torch.cuda.Stream()
+    for trial, (n_seq, lmax) in enumerate([(40, 300), (7, 1000), (1, 3), (300, 60)]):
+        lens = rng.integers(1, lmax - 1, n_seq)
+        T = n_seq * lmax + 17
+        valid = np.concatenate([r * lmax + 1 + np.arange(n) for r, n in enumerate(lens)]).astype(np.int64)
+        tok = np.concatenate([(1000 * trial + r) * 1024 + np.arange(n) for r, n in enumerate(lens)]).astype(np.int64)
+        ann = rng.integers(-1, 11, (valid.size, 4)).astype(np.int64)
+        ann[::5, 1] = ann[::5, 0]  # a class listed twice for one row
+        h = at.make_ctx(T, torch.from_numpy(valid), torch.from_numpy(tok), torch.from_numpy(ann))
+        d = at.make_ctx_device(T, torch.from_numpy(valid).pin_memory(), torch.from_numpy(tok).pin_memory(),
+                               torch.from_numpy(ann).pin_memory(), stream=side)
+        d.ready.synchronize()
+        assert (d.n_v, d.n_s, d.n_r) == (h.n_v, h.n_s, h.n_r)
+        for k in ("key", "rowmap32", "valid32", "sub_rows32", "res_rows32", "res_vidx32", "key_order32", "annT",
+                  "ann_counts"):
+            a, b = getattr(d, k), getattr(h, k)
+            assert a.shape == b.shape and torch.equal(a.cpu(), b.cpu()), (trial, k)
+        assert torch.equal(d.sub_idx.cpu(), h.sub_idx.cpu()) and torch.equal(d.res_in_sub.cpu(), h.res_in_sub.cpu())
+
+
+def test_stream_with_device_make_ctx_matches_reference():
+    """A golden stream with every context built by make_ctx_device on a side stream (as the prefetch
+    thread of run_atlas does): the reference's result, bit for bit."""
+    skw, ckw, seeded, _ = STREAM_CASES["bf16_seeded"]
+    z = golden("stream_bf16_seeded")
+    st = make_stream(**STREAM_SHAPE, **skw)
+    from proteus_b200.core import Atlas, AtlasConfig
+    at = Atlas(st.L, st.D, torch.from_numpy(z["E"]), AtlasConfig(**STREAM_CFG, **ckw),
+               n_annot=STREAM_SHAPE["n_annot"], device=DEV)
+    at.seed(torch.from_numpy(z["top_seed"]), torch.from_numpy(z["res_seed_key"]))
+    side = torch.cuda.Stream()
+    drive(at, st, to_input=lambda h: torch.from_numpy(h).to(DEV).to(torch.bfloat16),
+          make_ctx=lambda a, b: a.make_ctx_device(b.T, torch.from_numpy(b.valid_rows), torch.from_numpy(b.tok),
+                                                  torch.from_numpy(b.ann), stream=side))
+    at.check_errors()
+    bad = compare(at.result(), z, fields=EXACT_FIELDS)
+    assert not bad, bad

@@ -42,7 +42,13 @@ def _worker(rank, world, port, q):
         for k, v in list(vars(a).items()):
             if torch.is_tensor(v):
                 setattr(a, k, v.to(dev))
-        merge_states(a, gram=False)
+        # a Gram per rank (fp64 accumulator, already flushed): the combine must return the rank-order sum
+        grams = [torch.from_numpy(np.random.default_rng(r).standard_normal((2, 48, 48))) for r in range(world)]
+        a.gram = torch.zeros(2, 48, 48, device=dev)
+        a.gram64 = grams[rank].to(dev)
+        a.gram_rows = 100 + rank
+        a.flush_gram = lambda: None
+        merge_states(a, gram=True)
         torch.cuda.synchronize()
         want = {k[2:]: v for k, v in z.items() if k.startswith("m_")}
         L, D, K, B, Kr = 2, 48, 8, 5, 4
@@ -57,6 +63,8 @@ def _worker(rank, world, port, q):
             "ann_tot": np.array_equal(a.ann_tot.cpu().numpy(), want["ann_tot"]),
             "n": (a.n_seen, a.n_sub) == (int(want["n_seen"]), int(want["n_sub"])),
             "sums": np.allclose(a.sub_sum.cpu().numpy(), want["sub_sum"], rtol=1e-12, atol=1e-9),
+            "gram": np.array_equal(a.gram64.cpu().numpy(), (grams[0] + grams[1]).numpy()),
+            "gram_rows": a.gram_rows == 201,
         }
         q.put((rank, ok))
         torch.distributed.destroy_process_group()
@@ -83,3 +91,44 @@ def test_merge_states_two_gpus_nccl_matches_reference():
     for r in (0, 1):
         assert isinstance(out[r], dict), out[r]
         assert all(out[r].values()), out[r]
+
+
+def _run_atlas(args, nproc, cwd, env_extra=None):
+    import subprocess
+    import sys
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", **(env_extra or {}))
+    if nproc == 1:
+        cmd = [sys.executable, "-m", "proteus_b200.run_atlas", *args]
+    else:
+        cmd = ["timeout", "-k", "30", "840", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={nproc}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}", "-m",
+               "proteus_b200.run_atlas", *args]
+    r = subprocess.run(cmd, cwd=cwd, env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    return r.stdout
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_run_atlas_two_ranks_equals_one_rank(tmp_path):
+    """run_atlas under torchrun on two GPUs (each rank streams plan[rank::2], seeds from the global
+    stream, exact NCCL combine) gives the single-GPU run's atlas bit for bit; a two-rank run stopped
+    by --stop-after and resumed gives it too (both ranks stop at the same step)."""
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    base = ["--model", "8M", "--data", "synthetic:600:4", "--dtype", "bf16", "--tokens-per-batch", "8192",
+            "--pilot-tokens", "8192", "--K", "16", "--Kr", "8", "--seed-thresholds", "--ckpt-every", "3"]
+    one, two, part = tmp_path / "one", tmp_path / "two", tmp_path / "part"
+    _run_atlas(base + ["--device", "cuda:0", "--out", str(one)], 1, root)
+    _run_atlas(base + ["--out", str(two)], 2, root)
+    out = _run_atlas(base + ["--out", str(part), "--stop-after", "4"], 2, root)
+    assert "stopping after 4" in out
+    assert {p.name for p in (part / "ckpt").iterdir()} == {"rank0", "rank1"}
+    _run_atlas(base + ["--out", str(part), "--resume"], 2, root)
+    A = torch.load(one / "atlas.pt", weights_only=False)
+    for other in (two, part):
+        Bm = torch.load(other / "atlas.pt", weights_only=False)
+        for k in ("top_val", "top_tok", "res_tok", "res_key", "sub_bin", "enr", "ann_tot", "edges"):
+            assert torch.equal(A[k], Bm[k]), (other.name, k)
+        assert torch.equal(torch.nan_to_num(A["res_val"], nan=-7.0), torch.nan_to_num(Bm["res_val"], nan=-7.0))
+        assert A["n_seen"] == Bm["n_seen"] and A["n_sub"] == Bm["n_sub"]
+        assert torch.allclose(A["sub_sum"], Bm["sub_sum"], rtol=1e-9, atol=1e-9)

@@ -129,3 +129,14 @@ def test_prefetch_reraises_producer_errors_and_ends():
     q = Prefetch(iter([1, 2]), 1)
     assert list(q) == [1, 2]
     q.close()
+
+
+def test_overhead_summary_windows():
+    from proteus_b200.run_atlas import overhead_summary
+    paired = [(i, 10.0 if i < 60 else 0.2 + (i % 7) * 0.001) for i in range(5000)]
+    s = overhead_summary(paired)
+    assert s["paired_batches"] == 5000
+    assert s["prefix_0_59"]["n"] == 60 and s["prefix_0_59"]["median"] == 10.0
+    assert s["steady"]["n"] == 1600 and s["steady_from_batch"] == 3400 and abs(s["steady"]["median"] - 0.203) < 1e-9
+    assert set(s["windows"]) == {"0-100", "100-1000", "1000-3000", "3000-5000"}
+    assert overhead_summary([]) == {"paired_batches": 0}
