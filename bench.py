@@ -9,8 +9,9 @@ the length-bucketed batch plan (rank r takes batches r, r+N, ...; no communicati
 forward with the atlas hooks. A step is one batch of <= 32768 padded tokens: forward + per-layer
 filter / subsample statistics / enrichment / Gram staging / dense bursts + the end-of-batch merges.
   value  tokens/s (valid tokens, all ranks) with batch inputs resident in HBM, CUDA events, max over ranks
-  e2e    the same through the public API with host inputs: per step the H2D copy of the batch
-         (token ids, mask and the row context) from pinned memory and a D2H read of the atlas counters
+  e2e    the same through the public API with host inputs: per step the H2D copy of the raw batch
+         (token ids, mask, valid rows, token ids of the rows, annotation ids) from pinned memory, the
+         batch context built on the device (make_ctx_device), and a D2H read of the atlas counters
   roofline  the filter kernel (K1), timed live with CUDA events around every launch of the timed region
   cpu_baseline  the numpy oracle of the reference algorithm on the host, bounded sample
 Reference arm (--impl reference): the reference algorithm's CPU restatement (oracle) on the host cores,
@@ -809,28 +810,34 @@ def main():
         atlas.enabled = True
         fwd_ms = a2.elapsed_time(b2)
         del resident
-        # end to end through the public API: host inputs, H2D per step, D2H of the counters per step
+        # end to end through the public API: per step the raw batch (token ids, mask, valid rows, token
+        # ids of the rows, annotation ids) goes host -> device from pinned memory, the batch context is
+        # built on the device (make_ctx_device, on a side stream one step ahead, as run_atlas's prefetch
+        # thread does), the forward + atlas run, and the atlas counters come back to the host
         pinned = []
         h2d = 0
-        for bb, cc in e2e_host:
-            ids, am = bb.input_ids.pin_memory(), bb.attention_mask.pin_memory()
-            ctxp = cc.to("cpu")
-            for k, v in list(ctxp.__dict__.items()):
-                if torch.is_tensor(v):
-                    setattr(ctxp, k, v.pin_memory())
-            h2d += ids.numel() * 8 + am.numel() * 8 + sum(t.numel() * t.element_size() for t in ctx_tensors(ctxp))
-            pinned.append((ids, am, ctxp))
+        for bb, _ in e2e_host:
+            raw = [bb.input_ids.pin_memory(), bb.attention_mask.pin_memory(), bb.valid_rows.pin_memory(),
+                   bb.tok.pin_memory(), bb.ann.pin_memory()]
+            h2d += sum(t.numel() * t.element_size() for t in raw)
+            pinned.append((bb.n_rows, raw))
         out_host = torch.empty(4, dtype=torch.int64).pin_memory()
+        side = torch.cuda.Stream(device=dev)
         restore(atlas, snap)
         del snap
         barrier(world, local)
         torch.cuda.synchronize()
         a3, b3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a3.record()
-        for ids, am, ctxp in pinned:
-            ids_d, am_d = ids.to(dev, non_blocking=True), am.to(dev, non_blocking=True)
-            ctx_d = ctxp.to(dev, non_blocking=True)
+        mk = lambda j: atlas.make_ctx_device(pinned[j][0], pinned[j][1][2], pinned[j][1][3], pinned[j][1][4],  # noqa: E731
+                                             stream=side)
+        ctx_next = mk(0)
+        for j, (_, raw) in enumerate(pinned):
+            ids_d, am_d = raw[0].to(dev, non_blocking=True), raw[1].to(dev, non_blocking=True)
+            ctx_d = ctx_next
             step(model, atlas, ids_d, am_d, ctx_d)
+            if j + 1 < len(pinned):
+                ctx_next = mk(j + 1)
             out_host.copy_(atlas._dev_stats, non_blocking=True)
         b3.record()
         torch.cuda.synchronize()
@@ -898,6 +905,8 @@ def main():
                              "peak_source": peaks["source"]},
                 "gram_staged": {"launches": kt.count("gram"), "ms_total": kt.total_ms("gram"),
                                 "rows": kt.work.get("gram", 0)},
+                "atlas_kernels_in_step_ms": {k: kt.total_ms(k) / K for k in ("filter", "stats", "gram", "dense", "admit",
+                                                                           "merge")},
                 "dense_in_step": {"launches": kt.count("dense"), "ms_total": kt.total_ms("dense"),
                                   "triggered_layer_batches": stats1["dense_layer_batches"] - stats0.get("dense_layer_batches", 0)},
                 "device_status": atlas.device_status(),

@@ -521,10 +521,15 @@ class Atlas:
         if ann and KN.stats_enrich_supported(XT.dtype, self.B, len(levels), ctx.annT.shape[0]):
             # one pass over the staged rows: moments, bin masses and the enrichment contingencies,
             # the 0/1 masks built in shared memory for the int8 tensor-core contraction
+            kt = self.kernel_timer
+            if kt is not None:
+                kt.start("stats")
             with _rf("atlas.sub.kernel"):
                 KN.sub_stats_enrich_into(XT, col0, n, self.E[l, 0], self.E[l, 1], levels, self.sub_sum[l],
                                          self.sub_sq[l], self.sub_bin[l], ctx.annT,
                                          self.enr[l].view(2 * len(levels) * D, self.n_a), self.n_a, self._ws_se)
+            if kt is not None:
+                kt.stop("stats", work=n)
             if self.gram is not None:
                 self._stage_fill[l] += n8
                 if l == 0:
@@ -608,6 +613,9 @@ class Atlas:
             mode[filt] = 1
             cv, cr, cc = self._cand
             R = self._R if (c.reservoir and ctx.n_r) else None
+            kt = self.kernel_timer
+            if kt is not None:
+                kt.start("admit")
             with _rf("atlas.merge.cand"):
                 call("atlas_admit", L, D, B, c.K, c.Kr, self.U_res, int(bool(c.reservoir)), mode.data_ptr(),
                      ptr(self._counts), cap_main, cap_early if c.cap_frac_early > 0 else cap_main,
@@ -617,6 +625,11 @@ class Atlas:
                      ptr(self.res_s), ptr(self.res_seed), ptr(self.E), ptr(tg), ptr(tsc), ptr(tt), ptr(tv),
                      ptr(fl[L:L + 1]), tcap, ptr(rg), ptr(rsc), ptr(rt), ptr(rv), ptr(fl[L + 1:L + 2]), rcap,
                      ptr(fl[L + 2:L + 3]), st)
+            if kt is not None:
+                kt.stop("admit")
+        kt = self.kernel_timer
+        if kt is not None:
+            kt.start("merge")
         with _rf("atlas.merge.top"):
             KN.grouped_merge_records(self.top_k, self.top_t, self.top_s, c.K, tg, tsc, tt, tv, fl[L:L + 1], tcap,
                                      self._ws_top)
@@ -624,6 +637,8 @@ class Atlas:
             with _rf("atlas.merge.res"):
                 KN.grouped_merge_records(self.res_s, self.res_t, self.res_v, c.Kr, rg, rsc, rt, rv, fl[L + 1:L + 2],
                                          rcap, self._ws_res)
+        if kt is not None:
+            kt.stop("merge")
 
     def _count_batch(self, L, c, filt, fl, cap_main, cap_early):
         """Survivors of the non-overflowed filtered layers, records admitted, overflowed layers (each

@@ -10,7 +10,8 @@
 //      digits that are constant for bf16/fp16 inputs are skipped, and token ids are read only for
 //      elements tied on the whole value. Exactly min(K, n_v) batch elements reach the threshold; the
 //      state admission tests (s > seed, key > K-th state key) then apply.
-//    reservoir: the rows in ascending hash-key order (key_order) are split into one run per thread;
+//    reservoir: the rows in ascending hash-key order (key_order; their keys gathered once per launch
+//      into a sorted array) are split into one run per thread;
 //      each thread counts the admissible rows of its run per (pole, bin) (bin match and key under
 //      the bin's ceiling), a block scan turns the counts into global ranks, and the first Kr
 //      admissible rows of each bin are emitted. Runs that start above every ceiling stop at once.
@@ -73,6 +74,16 @@ __global__ void dense_gather_kernel(const T* __restrict__ H, int64_t D, int64_t 
   }
 }
 
+// Keys in key order (skey[j] = key[key_order[j]]), once per triggered launch: the reservoir walk of
+// every column then reads them sequentially instead of one random 8-byte load per row and column.
+__global__ void dense_sorted_keys_kernel(const int64_t* __restrict__ key, const int32_t* __restrict__ key_order,
+                                         int64_t n_v, int64_t* __restrict__ skey, const int32_t* __restrict__ count,
+                                         int64_t cap, int force) {
+  if (!triggered(count, cap, force)) return;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n_v; j += (int64_t)gridDim.x * blockDim.x)
+    skey[j] = key[key_order[j]];
+}
+
 // ---------------------------------------------------------------------------------------- column
 struct Staged {
   int32_t g[kStage];
@@ -124,7 +135,7 @@ template <int DT>
 __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T* scol, int64_t d,
                                              const typename Elem<DT>::T* __restrict__ HT,
                                              int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
-                                             const int64_t* __restrict__ key, const int32_t* __restrict__ key_order,
+                                             const int64_t* __restrict__ skey, const int32_t* __restrict__ key_order,
                                              int64_t layer, int64_t D, int B, int64_t K, int64_t Kr, int reservoir,
                                              const float* __restrict__ top_seed, const int64_t* __restrict__ top_k,
                                              const int64_t* __restrict__ res_s, const int64_t* __restrict__ res_seed,
@@ -329,10 +340,9 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
 #pragma unroll
     for (int b = 0; b < kMaxB; ++b) cnt[p][b] = 0;
   for (int64_t j = j0; j < j1; ++j) {
-    const int32_t vi = key_order[j];
-    const int64_t k = key[vi];
+    const int64_t k = skey[j];
     if (k >= maxceil) break;
-    const float h = Elem<DT>::f(col[vi]);
+    const float h = Elem<DT>::f(col[key_order[j]]);
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const float s = p ? -h : h;
@@ -373,9 +383,9 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
   }
   if (open) {
     for (int64_t j = j0; j < j1; ++j) {
-      const int32_t vi = key_order[j];
-      const int64_t k = key[vi];
+      const int64_t k = skey[j];
       if (k >= maxceil) break;
+      const int32_t vi = key_order[j];
       const float h = Elem<DT>::f(col[vi]);
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
@@ -402,7 +412,7 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
 template <int DT>
 __global__ void __launch_bounds__(kThreads)
 dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
-                    const int64_t* __restrict__ key, const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
+                    const int64_t* __restrict__ skey, const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
                     int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
                     const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
                     const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
@@ -414,7 +424,7 @@ dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, in
   auto* scol = col_in_smem ? reinterpret_cast<typename Elem<DT>::T*>(col_raw + ((sizeof(ColShared) + 15) / 16) * 16)
                            : nullptr;
   for (int64_t d = blockIdx.x; d < D; d += gridDim.x) {
-    dense_column<DT>(sh, scol, d, HT, ldh, n_v, tok, key, key_order, layer, D, B, K, Kr, reservoir, top_seed, top_k,
+    dense_column<DT>(sh, scol, d, HT, ldh, n_v, tok, skey, key_order, layer, D, B, K, Kr, reservoir, top_seed, top_k,
                      res_s, res_seed, E, top, res, err);
     __syncthreads();  // the next column re-initialises the shared state and the staged column
   }
@@ -434,6 +444,12 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   dense_gather_kernel<T><<<g1, dim3(32, 8), 0, st>>>(reinterpret_cast<const T*>(H), D, ld, valid_rows, n_v, n8, HT, n8,
                                                      count, cap, force);
   if (int e = check_launch("atlas_dense_select: gather")) return e;
+  // sorted keys after the transposed copy (16-byte aligned: D * n8 * esize is a multiple of 16)
+  int64_t* skey = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(scratch) + D * n8 * (int64_t)sizeof(T));
+  if (reservoir) {
+    dense_sorted_keys_kernel<<<grid_for(n_v, 256, 2), 256, 0, st>>>(key, key_order, n_v, skey, count, cap, force);
+    if (int e = check_launch("atlas_dense_select: sorted keys")) return e;
+  }
   // the column goes to shared memory when it fits next to the shared state (C4: ~62 KB of bf16 per
   // column, two CTAs per SM); otherwise it is read from the transposed copy in global memory
   const size_t base_smem = ((sizeof(ColShared) + 15) / 16) * 16;
@@ -448,7 +464,7 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
       per_sm < 1)
     per_sm = 1;
   const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
-  dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, key, key_order, layer, D, (int)B, K, Kr,
+  dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, skey, key_order, layer, D, (int)B, K, Kr,
                                                                 reservoir, top_seed, top_k, res_s, res_seed, E, count,
                                                                 cap, force, top, res, err, col_in_smem);
   return check_launch("atlas_dense_select: column");
@@ -463,7 +479,8 @@ using namespace atlas;
 
 extern "C" int64_t atlas_dense_scratch_bytes(int64_t n_v, int64_t D, int64_t B, int dtype) {
   (void)B;
-  return D * ((n_v + 7) / 8 * 8) * esize(dtype) + 256;
+  const int64_t n8 = (n_v + 7) / 8 * 8;
+  return D * n8 * esize(dtype) + n8 * 8 + 256;  // transposed valid rows, then the keys in key order
 }
 
 extern "C" int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, int64_t layer,

@@ -169,6 +169,8 @@ def parser():
     ap.add_argument("--profile-at", type=int, nargs="*", default=[])
     ap.add_argument("--max-batches", type=int, default=0)
     ap.add_argument("--deadline", type=float, default=0.0)
+    ap.add_argument("--host-ctx", action="store_true",
+                    help="build batch contexts with the host make_ctx (as the reference) instead of on the device")
     return ap
 
 
@@ -433,7 +435,12 @@ def main(argv=None):
                     prof = torch.profiler.profile(activities=acts)
                     prof.__enter__()
                 ta0 = time.time()
-                ctx = ctx_host.to(dev) if ctx_host is not None else atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann)
+                if ctx_host is not None:
+                    ctx = ctx_host.to(dev)
+                elif a.host_ctx:
+                    ctx = atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann)
+                else:
+                    ctx = atlas.make_ctx_device(b.n_rows, b.valid_rows, b.tok, b.ann)
                 n_before = atlas.n_seen
                 atlas.begin_batch(ctx)
                 model(input_ids=ids, attention_mask=am)
@@ -487,11 +494,20 @@ def main(argv=None):
                 return None
 
     prefetch = None
+    side = torch.cuda.Stream(device=torch.device(dev)) if not a.host_ctx else None
+
+    def with_ctx(b):
+        """The batch with its context: on the device (a side stream; the prefetch thread waits only
+        for it) or, with --host-ctx, built on the host as the reference does."""
+        if a.host_ctx:
+            return b, atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann, device="cpu")
+        return b, atlas.make_ctx_device(b.n_rows, b.valid_rows.pin_memory(), b.tok.pin_memory(),
+                                        b.ann.pin_memory() if b.ann is not None else None, stream=side)
+
     with torch.no_grad():
         src_iter = ds.batches(vocab, order, a.tokens_per_batch, plan=my_plan, start=start)
         if a.prefetch > 0:
-            prefetch = Prefetch(((b, atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann, device="cpu"))
-                                 for b in src_iter), a.prefetch)
+            prefetch = Prefetch((with_ctx(b) for b in src_iter), a.prefetch)
             src_iter = prefetch
         else:
             src_iter = iter((b, None) for b in src_iter)
