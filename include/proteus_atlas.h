@@ -91,10 +91,14 @@ int atlas_ctx_annotations(const int64_t* sub_idx, const int64_t* counts, const i
  *   kth     = max(res_s[g*B+b, Kr-1], res_seed[g*B+b]);  underfilled = kth < -U_res
  *   eps     = nextafter(min_b{E[g, b] : underfilled}, -inf)  (inf when none)
  *   thr[g]  = reservoir ? min(tau_top, eps) : tau_top            for g in [0, G)
+ * Optionally (non-NULL) it also keeps the batch's admission thresholds in compact arrays for
+ * atlas_admit: top_kth[g] = top_k[g, K-1] (top_k required) and, with reservoir,
+ * res_thr[g*B+b] = kth. They stay valid until the state is next merged (end of the batch).
  */
 int atlas_thresholds(const float* top_s, int64_t K, const int64_t* res_s, int64_t Kr,
                      const float* top_seed, const int64_t* res_seed, const float* E,
-                     int64_t G, int64_t B, int64_t U_res, int reservoir, float* thr, void* stream);
+                     int64_t G, int64_t B, int64_t U_res, int reservoir, float* thr,
+                     const int64_t* top_k, int64_t* top_kth, int64_t* res_thr, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * Subsample row gathers — replace H.index_select(0, sub_rows) and Hn.index_select(0, res_in_sub)
@@ -179,13 +183,15 @@ int atlas_batch_counters(const int32_t* count, int64_t L, const int8_t* filtered
 /* ------------------------------------------------------------------------------------------------
  * Candidate admission for the filtered layers of a batch — replaces _merge_filtered_impl's
  * candidate tests and the bulk-row paths _bulk_loop / _bulk_stacked (atlas/core.py:482-590).
+ * top_kth [G] and res_thr [G*B] are the batch's compact thresholds from atlas_thresholds
+ * (top_k[g, K-1] and max(res_s[g*B+b, Kr-1], res_seed[g*B+b])).
  * For every layer l with layer_mode[l] == 1 and count[l] <= cap(l):
  *   compacted candidate (h, row, col), pole p (s = +-h), g = (l*2+p)*D + col:
- *     top:  s > top_seed[g] && top_key(s, tok[row]) > top_k[g, K-1]      -> record (g, top_key, tok, s)
- *     res:  b = bin(s, E[l,p,col]) >= 0 && key[row] >= U_res && -key > max(res_s[g*B+b, Kr-1], res_seed)
+ *     top:  s > top_seed[g] && top_key(s, tok[row]) > top_kth[g]         -> record (g, top_key, tok, s)
+ *     res:  b = bin(s, E[l,p,col]) >= 0 && key[row] >= U_res && -key > res_thr[g*B+b]
  *                                                                        -> record (g*B+b, -key, tok, h)
  *   bulk rows R[l] [n_r, D] (rows with key < U_res; bulk_vidx = their valid-row indices):
- *     every (row, col, pole) with bin >= 0 and -key > max(res_s[.., Kr-1], res_seed) -> res record.
+ *     every (row, col, pole) with bin >= 0 and -key > res_thr[g*B+bin] -> res record.
  * cap(l) = l < early_layers ? cap_early : cap_main. Candidate buffers are [L, cand_stride].
  * Records are appended to SoA lists (group i32, score i64, tok i64, val f32) with device counters
  * n_top / n_res; an append past the list capacity sets err[0] and is dropped.
@@ -195,8 +201,7 @@ int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t 
                 int64_t early_layers, const float* cand_val, const int32_t* cand_row, const int32_t* cand_col,
                 int64_t cand_stride, const int64_t* tok, const int64_t* key,
                 const void* R, int dtype, int64_t n_r, int64_t r_stride, const int32_t* bulk_vidx,
-                const float* top_seed, const int64_t* top_k, const int64_t* res_s, const int64_t* res_seed,
-                const float* E,
+                const float* top_seed, const int64_t* top_kth, const int64_t* res_thr, const float* E,
                 int32_t* top_g, int64_t* top_sc, int64_t* top_tok, float* top_val, int32_t* n_top, int64_t top_cap,
                 int32_t* res_g, int64_t* res_sc, int64_t* res_tok, float* res_val, int32_t* n_res, int64_t res_cap,
                 int32_t* err, void* stream);

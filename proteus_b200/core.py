@@ -236,6 +236,10 @@ class Atlas:
         self._sub_done: set[int] = set()
         # per-batch device scratch (grown on demand)
         self.thr = torch.empty(L, 2, D, device=dev)
+        # the batch's admission thresholds, written by begin_batch: K-th top key per group, reservoir
+        # ceiling per bin (compact copies of top_k[:, K-1] and max(res_s[:, Kr-1], res_seed))
+        self._top_kth = torch.empty(G, dtype=torch.long, device=dev)
+        self._res_thr = torch.empty(G * B, dtype=torch.long, device=dev)
         self._counts = torch.zeros(L, dtype=torch.int32, device=dev)
         self._flags = torch.zeros(L + 4, dtype=torch.int32, device=dev)  # [0,L) dense ran; L: n_top; L+1: n_res; L+2: err
         self._cand = None
@@ -425,7 +429,7 @@ class Atlas:
         c = self.cfg
         call("atlas_thresholds", ptr(self.top_s), c.K, ptr(self.res_s), c.Kr, ptr(self.top_seed), ptr(self.res_seed),
              ptr(self.E), self.L * 2 * self.D, self.B, self.U_res, int(bool(c.reservoir)), ptr(self.thr),
-             stream_ptr(self.dev))
+             ptr(self.top_k), ptr(self._top_kth), ptr(self._res_thr), stream_ptr(self.dev))
 
     # ------------------------------------------------------------------ hook body
     @torch.no_grad()
@@ -621,8 +625,8 @@ class Atlas:
                      ptr(self._counts), cap_main, cap_early if c.cap_frac_early > 0 else cap_main,
                      c.early_layers if c.cap_frac_early > 0 else 0, ptr(cv), ptr(cr), ptr(cc), self._cand_cap,
                      ptr(ctx.tok), ptr(ctx.key), ptr(R), dtype_code(self._act_dtype), ctx.n_r if R is not None else 0,
-                     R.shape[1] if R is not None else 0, ptr(ctx.res_vidx32), ptr(self.top_seed), ptr(self.top_k),
-                     ptr(self.res_s), ptr(self.res_seed), ptr(self.E), ptr(tg), ptr(tsc), ptr(tt), ptr(tv),
+                     R.shape[1] if R is not None else 0, ptr(ctx.res_vidx32), ptr(self.top_seed), ptr(self._top_kth),
+                     ptr(self._res_thr), ptr(self.E), ptr(tg), ptr(tsc), ptr(tt), ptr(tv),
                      ptr(fl[L:L + 1]), tcap, ptr(rg), ptr(rsc), ptr(rt), ptr(rv), ptr(fl[L + 1:L + 2]), rcap,
                      ptr(fl[L + 2:L + 3]), st)
             if kt is not None:

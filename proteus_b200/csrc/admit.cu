@@ -44,72 +44,83 @@ __device__ __forceinline__ float ld_elem<__nv_bfloat16>(const __nv_bfloat16* p) 
 template <>
 __device__ __forceinline__ float ld_elem<__half>(const __half* p) { return __half2float(*p); }
 
-template <typename RT>
+// Compacted candidates of every admitted layer in one flattened index space (a CTA first builds the
+// prefix of the layers' candidate counts in shared memory), so every warp of the grid works on some
+// layer's candidates at once instead of the layers taking turns. The state tests read the batch's
+// compact thresholds: the group's K-th top key and the bin's ceiling max(res_s[., Kr-1], res_seed).
 __global__ void __launch_bounds__(256)
-admit_kernel(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t U_res, int reservoir, uint64_t mode_mask,
+admit_kernel(int64_t L, int64_t D, int64_t B, int64_t U_res, int reservoir, uint64_t mode_mask,
              const int32_t* __restrict__ count, int64_t cap_main, int64_t cap_early, int64_t early_layers,
              const float* __restrict__ cval, const int32_t* __restrict__ crow, const int32_t* __restrict__ ccol,
              int64_t cstride, const int64_t* __restrict__ tok, const int64_t* __restrict__ key,
-             const RT* __restrict__ R, int64_t n_r, int64_t r_stride, const int32_t* __restrict__ bulk_vidx,
-             const float* __restrict__ top_seed, const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
-             const int64_t* __restrict__ res_seed, const float* __restrict__ E, Lists o) {
+             const float* __restrict__ top_seed, const int64_t* __restrict__ top_kth,
+             const int64_t* __restrict__ res_thr, const float* __restrict__ E, Lists o) {
+  __shared__ int64_t s_start[65];
   const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    int64_t acc = 0;
+    for (int64_t l = 0; l < L; ++l) {
+      s_start[l] = acc;
+      if ((mode_mask >> l) & 1) {
+        const int64_t cap = l < early_layers ? cap_early : cap_main;
+        const int64_t c = count[l];
+        if (c <= cap) acc += c;  // an overflowed layer went through the dense path
+      }
+    }
+    s_start[L] = acc;
+  }
+  __syncthreads();
+  const int64_t total = s_start[L];
   const int64_t warp_id = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t l = 0; l < L; ++l) {
-    if (!((mode_mask >> l) & 1)) continue;
-    const int64_t cap = l < early_layers ? cap_early : cap_main;
-    const int64_t c = count[l];
-    if (c > cap) continue;  // overflowed: this layer went through the dense path
-    // ---- compacted candidates
-    for (int64_t base = warp_id * 32; base < c; base += n_warps * 32) {
-      const int64_t i = base + lane;
-      int nt = 0, nr = 0;
-      int32_t tg[2], rg[2];
-      int64_t tsc[2], rsc[2], tt[2], rt[2];
-      float tv[2], rv[2];
-      if (i < c) {
-        const float h = cval[l * cstride + i];
-        const int32_t row = crow[l * cstride + i];
-        const int64_t col = ccol[l * cstride + i];
-        const int64_t tk = tok[row], ky = key[row];
+  for (int64_t base = warp_id * 32; base < total; base += n_warps * 32) {
+    const int64_t f = base + lane;
+    int nt = 0, nr = 0;
+    int32_t tg[2], rg[2];
+    int64_t tsc[2], rsc[2], tt[2], rt[2];
+    float tv[2], rv[2];
+    if (f < total) {
+      int lo = 0, hi = (int)L;  // the layer whose range holds f: last l with s_start[l] <= f
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_start[mid] <= f) lo = mid; else hi = mid;
+      }
+      const int64_t l = lo, i = f - s_start[lo];
+      const float h = cval[l * cstride + i];
+      const int32_t row = crow[l * cstride + i];
+      const int64_t col = ccol[l * cstride + i];
+      const int64_t tk = tok[row], ky = key[row];
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const float s = p ? -h : h;
-          const int64_t g = (l * 2 + p) * D + col;
-          if (s > top_seed[g]) {
-            const int64_t k64 = top_key(s, tk);
-            if (k64 > top_k[g * K + (K - 1)]) {
-              tg[nt] = (int32_t)g; tsc[nt] = k64; tt[nt] = tk; tv[nt] = s; ++nt;
-            }
+      for (int p = 0; p < 2; ++p) {
+        const float s = p ? -h : h;
+        const int64_t g = (l * 2 + p) * D + col;
+        if (s > top_seed[g]) {
+          const int64_t k64 = top_key(s, tk);
+          if (k64 > top_kth[g]) {
+            tg[nt] = (int32_t)g; tsc[nt] = k64; tt[nt] = tk; tv[nt] = s; ++nt;
           }
-          if (reservoir && ky >= U_res) {
-            const int b = bin_of(s, E + g * B, (int)B);
-            if (b >= 0) {
-              const int64_t gr = g * B + b;
-              int64_t thr = res_s[gr * Kr + (Kr - 1)];
-              const int64_t sd = res_seed[gr];
-              if (sd > thr) thr = sd;
-              if (-ky > thr) {
-                rg[nr] = (int32_t)gr; rsc[nr] = -ky; rt[nr] = tk; rv[nr] = h; ++nr;
-              }
+        }
+        if (reservoir && ky >= U_res) {
+          const int b = bin_of(s, E + g * B, (int)B);
+          if (b >= 0) {
+            const int64_t gr = g * B + b;
+            if (-ky > res_thr[gr]) {
+              rg[nr] = (int32_t)gr; rsc[nr] = -ky; rt[nr] = tk; rv[nr] = h; ++nr;
             }
           }
         }
       }
-      warp_append(lane, nt, tg, tsc, tt, tv, o.tg, o.tsc, o.ttok, o.tval, o.nt, o.tcap, o.err);
-      warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
     }
+    warp_append(lane, nt, tg, tsc, tt, tv, o.tg, o.tsc, o.ttok, o.tval, o.nt, o.tcap, o.err);
+    warp_append(lane, nr, rg, rsc, rt, rv, o.rg, o.rsc, o.rtok, o.rval, o.nr, o.rcap, o.err);
   }
 }
 
 // Bulk rows (key < U_res; every element is a reservoir candidate). A CTA takes one layer, 256
-// columns and a chunk of up to kAdmRows rows. It first loads its columns' reservoir thresholds
-// (max of the Kr-th state key and the seed, both poles, every bin) into a shared-memory table and
+// columns and a chunk of up to kAdmRows rows. It first copies its columns' reservoir ceilings
+// (both poles, every bin; contiguous in the batch's compact array) into a shared-memory table and
 // the chunk's row keys into shared memory; each thread then holds one column's bin edges in
-// registers and walks the rows (R read coalesced along the columns). Fetching the threshold of
-// each element from global memory instead costs a scattered 8-byte read per element and pole (a
-// 32-byte sector per lane), which dominated the admission time.
+// registers and walks the rows (R read coalesced along the columns).
 constexpr int kAdmB = 8;
 constexpr int kAdmRows = 64;  // most bulk rows per CTA (grid z); fewer when that leaves the GPU short of CTAs
 constexpr int kAdmCols = 256;
@@ -119,8 +130,8 @@ __global__ void __launch_bounds__(kAdmCols)
 admit_bulk_kernel(int64_t L, int64_t D, int64_t Kr, uint64_t mode_mask, const int32_t* __restrict__ count,
                   int64_t cap_main, int64_t cap_early, int64_t early_layers, const int64_t* __restrict__ tok,
                   const int64_t* __restrict__ key, const RT* __restrict__ R, int64_t n_r, int64_t r_stride,
-                  const int32_t* __restrict__ bulk_vidx, const int64_t* __restrict__ res_s,
-                  const int64_t* __restrict__ res_seed, const float* __restrict__ E, int rows_per_cta, Lists o) {
+                  const int32_t* __restrict__ bulk_vidx, const int64_t* __restrict__ res_thr,
+                  const float* __restrict__ E, int rows_per_cta, Lists o) {
   const int lane = threadIdx.x & 31;
   const int64_t col = (int64_t)blockIdx.x * kAdmCols + threadIdx.x;
   const int64_t l = blockIdx.y;
@@ -140,14 +151,7 @@ admit_bulk_kernel(int64_t L, int64_t D, int64_t Kr, uint64_t mode_mask, const in
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       e[p][b] = ok ? E[g * NB + b] : __int_as_float(0x7F800000);  // +inf: never reached
-      int64_t t = INT64_MAX;
-      if (ok) {
-        const int64_t gr = g * NB + b;
-        t = res_s[gr * Kr + (Kr - 1)];
-        const int64_t sd = res_seed[gr];
-        if (sd > t) t = sd;
-      }
-      s_thr[p][b][threadIdx.x] = t;
+      s_thr[p][b][threadIdx.x] = ok ? res_thr[g * NB + b] : INT64_MAX;
     }
   }
   if (threadIdx.x < nrows) {
@@ -195,23 +199,22 @@ admit_bulk_kernel(int64_t L, int64_t D, int64_t Kr, uint64_t mode_mask, const in
 template <typename RT, int NB>
 void launch_admit_bulk(dim3 gb, cudaStream_t st, int64_t L, int64_t D, int64_t Kr, uint64_t mask, const int32_t* count,
                        int64_t cap_main, int64_t cap_early, int64_t early_layers, const int64_t* tok, const int64_t* key,
-                       const void* R, int64_t n_r, int64_t r_stride, const int32_t* bulk_vidx, const int64_t* res_s,
-                       const int64_t* res_seed, const float* E, int rows_per_cta, Lists o) {
+                       const void* R, int64_t n_r, int64_t r_stride, const int32_t* bulk_vidx, const int64_t* res_thr,
+                       const float* E, int rows_per_cta, Lists o) {
   admit_bulk_kernel<RT, NB><<<gb, kAdmCols, 0, st>>>(L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key,
-                                                    (const RT*)R, n_r, r_stride, bulk_vidx, res_s, res_seed, E,
-                                                    rows_per_cta, o);
+                                                    (const RT*)R, n_r, r_stride, bulk_vidx, res_thr, E, rows_per_cta,
+                                                    o);
 }
 
 template <typename RT>
 int launch_admit_bulk_b(int64_t B, dim3 gb, cudaStream_t st, int64_t L, int64_t D, int64_t Kr, uint64_t mask,
                         const int32_t* count, int64_t cap_main, int64_t cap_early, int64_t early_layers,
                         const int64_t* tok, const int64_t* key, const void* R, int64_t n_r, int64_t r_stride,
-                        const int32_t* bulk_vidx, const int64_t* res_s, const int64_t* res_seed, const float* E,
-                        int rows_per_cta, Lists o) {
+                        const int32_t* bulk_vidx, const int64_t* res_thr, const float* E, int rows_per_cta, Lists o) {
 #define ATLAS_ADMIT_B(NBV)                                                                                           \
   case NBV:                                                                                                         \
     launch_admit_bulk<RT, NBV>(gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key, R, n_r,  \
-                               r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);                           \
+                               r_stride, bulk_vidx, res_thr, E, rows_per_cta, o);                                   \
     return ATLAS_OK;
   switch (B) {
     ATLAS_ADMIT_B(1) ATLAS_ADMIT_B(2) ATLAS_ADMIT_B(3) ATLAS_ADMIT_B(4)
@@ -231,10 +234,10 @@ extern "C" int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t K
                            int64_t early_layers, const float* cand_val, const int32_t* cand_row, const int32_t* cand_col,
                            int64_t cand_stride, const int64_t* tok, const int64_t* key, const void* R, int dtype,
                            int64_t n_r, int64_t r_stride, const int32_t* bulk_vidx, const float* top_seed,
-                           const int64_t* top_k, const int64_t* res_s, const int64_t* res_seed, const float* E,
-                           int32_t* top_g, int64_t* top_sc, int64_t* top_tok, float* top_val, int32_t* n_top,
-                           int64_t top_cap, int32_t* res_g, int64_t* res_sc, int64_t* res_tok, float* res_val,
-                           int32_t* n_res, int64_t res_cap, int32_t* err, void* stream) {
+                           const int64_t* top_kth, const int64_t* res_thr, const float* E, int32_t* top_g,
+                           int64_t* top_sc, int64_t* top_tok, float* top_val, int32_t* n_top, int64_t top_cap,
+                           int32_t* res_g, int64_t* res_sc, int64_t* res_tok, float* res_val, int32_t* n_res,
+                           int64_t res_cap, int32_t* err, void* stream) {
   ATLAS_REQUIRE(L >= 0 && L <= 64, "admit: L must be 0..64");
   ATLAS_REQUIRE(D > 0 && B >= 1 && K >= 1 && Kr >= 1 && n_r >= 0 && r_stride >= n_r, "admit: bad sizes");
   ATLAS_REQUIRE(2 * L * D * B < (1LL << 31), "admit: group ids exceed int32");
@@ -242,36 +245,19 @@ extern "C" int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t K
   for (int64_t l = 0; l < L; ++l)
     if (layer_mode_host && layer_mode_host[l]) mask |= 1ull << l;
   if (mask == 0) return ATLAS_OK;
-  ATLAS_REQUIRE(count && cand_val && cand_row && cand_col && tok && key && top_seed && top_k && n_top && top_g &&
+  ATLAS_REQUIRE(count && cand_val && cand_row && cand_col && tok && key && top_seed && top_kth && n_top && top_g &&
                     top_sc && top_tok && top_val && err,
                 "admit: null pointer");
-  ATLAS_REQUIRE(!reservoir || (res_s && res_seed && E && res_g && res_sc && res_tok && res_val && n_res),
+  ATLAS_REQUIRE(!reservoir || (res_thr && E && res_g && res_sc && res_tok && res_val && n_res),
                 "admit: null reservoir pointer");
   ATLAS_REQUIRE(!reservoir || n_r == 0 || (R && bulk_vidx), "admit: bulk rows missing");
   Lists o{top_g, top_sc, top_tok, top_val, n_top, top_cap, res_g, res_sc, res_tok, res_val, n_res, res_cap, err};
   ATLAS_REQUIRE(B <= kAdmB, "admit: at most %d bins", kAdmB);
-  const int64_t work = cap_main > cap_early ? cap_main : cap_early;
-  const unsigned grid = grid_for(work, 256, 8);
+  const int64_t per_layer = cap_main > cap_early ? cap_main : cap_early;
+  const unsigned grid = grid_for(per_layer * L, 256, 8);
   cudaStream_t st = (cudaStream_t)stream;
-  switch (dtype) {
-    case ATLAS_BF16:
-      admit_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(L, D, B, K, Kr, U_res, reservoir, mask, count, cap_main, cap_early,
-          early_layers, cand_val, cand_row, cand_col, cand_stride, tok, key, (const __nv_bfloat16*)R, n_r, r_stride,
-          bulk_vidx, top_seed, top_k, res_s, res_seed, E, o);
-      break;
-    case ATLAS_F16:
-      admit_kernel<__half><<<grid, 256, 0, st>>>(L, D, B, K, Kr, U_res, reservoir, mask, count, cap_main, cap_early,
-          early_layers, cand_val, cand_row, cand_col, cand_stride, tok, key, (const __half*)R, n_r, r_stride, bulk_vidx,
-          top_seed, top_k, res_s, res_seed, E, o);
-      break;
-    case ATLAS_F32:
-      admit_kernel<float><<<grid, 256, 0, st>>>(L, D, B, K, Kr, U_res, reservoir, mask, count, cap_main, cap_early,
-          early_layers, cand_val, cand_row, cand_col, cand_stride, tok, key, (const float*)R, n_r, r_stride, bulk_vidx,
-          top_seed, top_k, res_s, res_seed, E, o);
-      break;
-    default:
-      return fail(ATLAS_ERR_ARG, "admit: unknown dtype %d", dtype);
-  }
+  admit_kernel<<<grid, 256, 0, st>>>(L, D, B, U_res, reservoir, mask, count, cap_main, cap_early, early_layers, cand_val,
+                                     cand_row, cand_col, cand_stride, tok, key, top_seed, top_kth, res_thr, E, o);
   if (int e = check_launch("atlas_admit")) return e;
   if (!reservoir || n_r == 0) return ATLAS_OK;
   // rows per CTA: up to kAdmRows (the column's thresholds are loaded once per CTA), but at least about
@@ -286,16 +272,18 @@ extern "C" int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t K
   switch (dtype) {
     case ATLAS_BF16:
       e2 = launch_admit_bulk_b<__nv_bfloat16>(B, gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok,
-                                              key, R, n_r, r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);
+                                              key, R, n_r, r_stride, bulk_vidx, res_thr, E, rows_per_cta, o);
       break;
     case ATLAS_F16:
       e2 = launch_admit_bulk_b<__half>(B, gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key, R,
-                                       n_r, r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);
+                                       n_r, r_stride, bulk_vidx, res_thr, E, rows_per_cta, o);
+      break;
+    case ATLAS_F32:
+      e2 = launch_admit_bulk_b<float>(B, gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key, R,
+                                      n_r, r_stride, bulk_vidx, res_thr, E, rows_per_cta, o);
       break;
     default:
-      e2 = launch_admit_bulk_b<float>(B, gb, st, L, D, Kr, mask, count, cap_main, cap_early, early_layers, tok, key, R,
-                                      n_r, r_stride, bulk_vidx, res_s, res_seed, E, rows_per_cta, o);
-      break;
+      return fail(ATLAS_ERR_ARG, "admit: unknown dtype %d", dtype);
   }
   if (e2) return e2;
   return check_launch("atlas_admit: bulk rows");

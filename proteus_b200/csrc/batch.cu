@@ -8,13 +8,17 @@ namespace {
 // ---------------------------------------------------------------------------- thresholds
 // One thread per (layer, pole, column) group; reads the K-th slot of the top-K state and the Kr-th
 // slot of the B reservoirs (core.py:250-259).
+// With top_kth / res_thr it also keeps, for the batch's admission, each group's K-th state key and
+// each bin's admission ceiling max(res_s[., Kr-1], res_seed) in compact arrays.
 __global__ void thresholds_kernel(const float* __restrict__ top_s, int64_t K, const int64_t* __restrict__ res_s,
                                   int64_t Kr, const float* __restrict__ top_seed, const int64_t* __restrict__ res_seed,
                                   const float* __restrict__ E, int64_t G, int64_t B, int64_t U_res, int reservoir,
-                                  float* __restrict__ thr) {
+                                  float* __restrict__ thr, const int64_t* __restrict__ top_k,
+                                  int64_t* __restrict__ top_kth, int64_t* __restrict__ res_thr) {
   for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < G; g += (int64_t)gridDim.x * blockDim.x) {
     const float tau = top_s[g * K + (K - 1)];
     const float tau_top = fmaxf(next_down(tau), top_seed[g]);
+    if (top_kth) top_kth[g] = top_k[g * K + (K - 1)];
     if (!reservoir) {
       thr[g] = tau_top;
       continue;
@@ -25,6 +29,7 @@ __global__ void thresholds_kernel(const float* __restrict__ top_s, int64_t K, co
       int64_t kth = res_s[gb * Kr + (Kr - 1)];
       const int64_t sd = res_seed[gb];
       if (sd > kth) kth = sd;
+      if (res_thr) res_thr[gb] = kth;
       if (kth < -U_res) eps = fminf(eps, E[gb]);
     }
     thr[g] = fminf(tau_top, next_down(eps));
@@ -405,13 +410,16 @@ extern "C" int atlas_batch_counters(const int32_t* count, int64_t L, const int8_
 
 extern "C" int atlas_thresholds(const float* top_s, int64_t K, const int64_t* res_s, int64_t Kr, const float* top_seed,
                                 const int64_t* res_seed, const float* E, int64_t G, int64_t B, int64_t U_res,
-                                int reservoir, float* thr, void* stream) {
+                                int reservoir, float* thr, const int64_t* top_k, int64_t* top_kth, int64_t* res_thr,
+                                void* stream) {
   ATLAS_REQUIRE(K >= 1 && Kr >= 1 && G >= 0 && B >= 1, "thresholds: bad sizes K=%lld Kr=%lld G=%lld B=%lld",
                 (long long)K, (long long)Kr, (long long)G, (long long)B);
   if (G == 0) return ATLAS_OK;
   ATLAS_REQUIRE(top_s && top_seed && thr && (!reservoir || (res_s && res_seed && E)), "thresholds: null pointer");
+  ATLAS_REQUIRE(!top_kth || top_k, "thresholds: top_kth needs top_k");
   thresholds_kernel<<<grid_for(G, 256), 256, 0, (cudaStream_t)stream>>>(top_s, K, res_s, Kr, top_seed, res_seed, E, G,
-                                                                        B, U_res, reservoir, thr);
+                                                                        B, U_res, reservoir, thr, top_k, top_kth,
+                                                                        reservoir ? res_thr : nullptr);
   return check_launch("atlas_thresholds");
 }
 

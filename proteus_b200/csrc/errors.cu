@@ -31,4 +31,4 @@ int check_launch(const char* what) {
 }  // namespace atlas
 
 extern "C" const char* atlas_last_error(void) { return atlas::g_err; }
-extern "C" int atlas_abi_version(void) { return 1; }
+extern "C" int atlas_abi_version(void) { return 2; }
