@@ -456,13 +456,20 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   const size_t col_bytes = (size_t)n8 * sizeof(T);
   const int col_in_smem = base_smem + col_bytes <= (size_t)kDenseSmemMax ? 1 : 0;
   const size_t smem = col_in_smem ? base_smem + col_bytes : sizeof(ColShared);
-  if (cudaFuncSetAttribute(dense_column_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDenseSmemMax) !=
-      cudaSuccess)
-    return fail(ATLAS_ERR_CUDA, "dense_select: cannot reserve %zu bytes of shared memory", smem);
-  int per_sm = 0;  // resident CTAs per SM at this shared-memory size
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dense_column_kernel<DT>, kThreads, smem) != cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
+  // the attribute is set once per device and instantiation (this launch runs once per layer and
+  // batch, mostly to exit at once on the device, so no per-call host queries)
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    if (cudaFuncSetAttribute(dense_column_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDenseSmemMax) !=
+        cudaSuccess)
+      return fail(ATLAS_ERR_CUDA, "dense_select: cannot reserve %zu bytes of shared memory", smem);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  // resident CTAs per SM: registers allow two (127 x 256 per CTA); shared memory allows two while
+  // both fit in the SM's 228 KB (1 KB of it reserved per CTA)
+  const int per_sm = (2 * (smem + 1024) <= (size_t)228 * 1024) ? 2 : 1;
   const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
   dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, skey, key_order, layer, D, (int)B, K, Kr,
                                                                 reservoir, top_seed, top_k, res_s, res_seed, E, count,

@@ -527,11 +527,13 @@ int launch_bulk(const void* H, int64_t T, int64_t D, int64_t ld, const int32_t* 
                 (long long)D);
   const size_t smem = sizeof(BulkSmem) + 128;
   static_assert(kBCtasPerSm * (sizeof(BulkSmem) + 128 + 1024) <= 228 * 1024, "bulk filter: CTAs do not fit an SM");
-  static bool attr_set = false;
-  if (!attr_set) {
+  static bool attr_set[64] = {};  // per device: a function attribute belongs to one device's context
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     if (cudaFuncSetAttribute(filter_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return fail(ATLAS_ERR_CUDA, "filter: cannot reserve %zu bytes of shared memory", smem);
-    attr_set = true;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   CUtensorMap tm;
   if (int e = make_tmap_2d(&tm, H, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)D, (uint64_t)T, (uint64_t)ld * 2,

@@ -937,9 +937,15 @@ int launch_stats_enrich_b(const __nv_bfloat16* XT, int64_t ldx, int64_t col0, in
   unsigned int* tickets = reinterpret_cast<unsigned int*>(ws);
   double* part = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(ws) + ((dtiles * 4 + 255) / 256) * 256);
   const size_t smem = sizeof(SESmem<AP>) + 1024;
-  if (cudaFuncSetAttribute(stats_enrich_kernel<AP, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess)
-    return fail(ATLAS_ERR_CUDA, "sub_stats_enrich: cannot reserve %zu bytes of shared memory", smem);
+  static bool attr_set[64] = {};  // once per device and instantiation (one launch per layer and batch)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    if (cudaFuncSetAttribute(stats_enrich_kernel<AP, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return fail(ATLAS_ERR_CUDA, "sub_stats_enrich: cannot reserve %zu bytes of shared memory", smem);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
   uint32_t tcols = 32;
   while (tcols < (uint32_t)(2 * NL * AP)) tcols <<= 1;
   stats_enrich_kernel<AP, NB><<<dim3((unsigned)dtiles, (unsigned)ks), SE_THREADS, smem, st>>>(
