@@ -126,6 +126,8 @@ struct ColShared {
   int need[2], nbits[2], done[2];
   int cand[2];                            // admissible top-K candidates per pole
   int scan[kThreads / 32][2 * kMaxB];
+  int64_t ceil[2 * kMaxB];                // reservoir key ceiling per (pole, bin) of the column
+  uint16_t rcnt[2 * kMaxB][kThreads];     // per thread and (pole, bin): count, then start rank
   int base;
   Staged st;
 };
@@ -311,34 +313,35 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
   flush(sh.st, top, err, &sh.base);
   if (!reservoir) return;
   // ------------------------------------------------------------------ reservoir bottom-Kr
+  // Bin edges in registers; each (pole, bin) slot c = p*kMaxB + b has its key ceiling in shared
+  // memory, and each thread its count (then its start rank) per slot in shared memory, so a row
+  // costs one shared load / store for its own slot instead of a compare-and-select over all slots.
+  // A row belongs to at most the pole whose lowest edge it reaches (both only on a tie with it).
   float e[2][kMaxB];
-  int64_t ceil[2][kMaxB];
   int64_t maxceil = 0;
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
 #pragma unroll
     for (int b = 0; b < kMaxB; ++b) {
-      e[p][b] = __int_as_float(0x7F800000);
-      ceil[p][b] = 0;
+      e[p][b] = __int_as_float(0x7FC00000);  // NaN: an unused edge compares false, even for +inf
+      int64_t c = 0;
       if (b < B) {
         const int64_t gr = ((layer * 2 + p) * D + d) * B + b;
         e[p][b] = E[gr];
         int64_t th = res_s[gr * Kr + (Kr - 1)];
         const int64_t sd = res_seed[gr];
         if (sd > th) th = sd;
-        ceil[p][b] = (th == kI64Min) ? (1ll << 32) : -th;  // admit key < ceil
-        if (ceil[p][b] > maxceil) maxceil = ceil[p][b];
+        c = (th == kI64Min) ? (1ll << 32) : -th;  // admit key < ceil
+        if (c > maxceil) maxceil = c;
       }
+      if (tid == 0) sh.ceil[p * kMaxB + b] = c;
     }
   }
+  for (int c = 0; c < 2 * kMaxB; ++c) sh.rcnt[c][tid] = 0;
+  __syncthreads();
   const int64_t run = (n_v + kThreads - 1) / kThreads;
   const int64_t j0 = tid * run;
   const int64_t j1 = j0 + run < n_v ? j0 + run : n_v;
-  int cnt[2][kMaxB];
-#pragma unroll
-  for (int p = 0; p < 2; ++p)
-#pragma unroll
-    for (int b = 0; b < kMaxB; ++b) cnt[p][b] = 0;
   for (int64_t j = j0; j < j1; ++j) {
     const int64_t k = skey[j];
     if (k >= maxceil) break;
@@ -346,40 +349,40 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
       const float s = p ? -h : h;
-      int bin = -1;
+      if (!(s >= e[p][0])) continue;
+      int bin = 0;
 #pragma unroll
-      for (int b = 0; b < kMaxB; ++b) bin += (b < B && s >= e[p][b]) ? 1 : 0;
-#pragma unroll
-      for (int b = 0; b < kMaxB; ++b)
-        if (b == bin && k < ceil[p][b] && cnt[p][b] < Kr) cnt[p][b]++;
-    }
-  }
-  // block exclusive scan of the per-thread counts, for every (pole, bin)
-  int start[2][kMaxB];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-#pragma unroll
-    for (int b = 0; b < kMaxB; ++b) {
-      const int v = cnt[p][b];
-      int incl = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
+      for (int b = 1; b < kMaxB; ++b) bin += (s >= e[p][b]) ? 1 : 0;
+      const int c = p * kMaxB + bin;
+      if (k < sh.ceil[c]) {
+        const int n = sh.rcnt[c][tid];
+        if (n < Kr) sh.rcnt[c][tid] = (uint16_t)(n + 1);
       }
-      if (lane == 31) sh.scan[warp][p * kMaxB + b] = incl;
-      start[p][b] = incl - v;
     }
   }
-  __syncthreads();
+  // block exclusive scan of the per-thread counts, for every (pole, bin); the start ranks replace
+  // the counts in place
   bool open = false;
 #pragma unroll
-  for (int p = 0; p < 2; ++p) {
+  for (int c = 0; c < 2 * kMaxB; ++c) {
+    const int v = sh.rcnt[c][tid];
+    int incl = v;
 #pragma unroll
-    for (int b = 0; b < kMaxB; ++b) {
-      for (int w = 0; w < warp; ++w) start[p][b] += sh.scan[w][p * kMaxB + b];
-      open |= (b < B && cnt[p][b] > 0 && start[p][b] < Kr);
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
     }
+    if (lane == 31) sh.scan[warp][c] = incl;
+    sh.rcnt[c][tid] = (uint16_t)(incl - v);  // within-warp start, completed below
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < 2 * kMaxB; ++c) {
+    int st = sh.rcnt[c][tid];
+    for (int w = 0; w < warp; ++w) st += sh.scan[w][c];
+    const int b = c % kMaxB;
+    open |= (b < B && st < Kr);
+    sh.rcnt[c][tid] = (uint16_t)(st < 65535 ? st : 65535);
   }
   if (open) {
     for (int64_t j = j0; j < j1; ++j) {
@@ -390,15 +393,16 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const float s = p ? -h : h;
-        int bin = -1;
+        if (!(s >= e[p][0])) continue;
+        int bin = 0;
 #pragma unroll
-        for (int b = 0; b < kMaxB; ++b) bin += (b < B && s >= e[p][b]) ? 1 : 0;
-#pragma unroll
-        for (int b = 0; b < kMaxB; ++b) {
-          if (b == bin && k < ceil[p][b]) {
-            if (start[p][b] < Kr)
-              stage(sh.st, (int32_t)(((layer * 2 + p) * D + d) * B + b), -k, tok[vi], h, err);
-            start[p][b]++;
+        for (int b = 1; b < kMaxB; ++b) bin += (s >= e[p][b]) ? 1 : 0;
+        const int c = p * kMaxB + bin;
+        if (k < sh.ceil[c]) {
+          const int st = sh.rcnt[c][tid];
+          if (st < Kr) {
+            stage(sh.st, (int32_t)(((layer * 2 + p) * D + d) * B + bin), -k, tok[vi], h, err);
+            sh.rcnt[c][tid] = (uint16_t)(st + 1);
           }
         }
       }
@@ -410,7 +414,7 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
 // Columns are taken grid-stride by at most one resident wave of CTAs, so an untriggered launch costs
 // about a wave of early exits rather than one CTA per column.
 template <int DT>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
                     const int64_t* __restrict__ skey, const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
                     int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
@@ -467,9 +471,10 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
       return fail(ATLAS_ERR_CUDA, "dense_select: cannot reserve %zu bytes of shared memory", smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  // resident CTAs per SM: registers allow two (127 x 256 per CTA); shared memory allows two while
-  // both fit in the SM's 228 KB (1 KB of it reserved per CTA)
-  const int per_sm = (2 * (smem + 1024) <= (size_t)228 * 1024) ? 2 : 1;
+  // resident CTAs per SM: registers allow four (at most 64 x 256 per CTA); shared memory as many as
+  // fit in the SM's 228 KB (1 KB of it reserved per CTA)
+  int per_sm = (int)(((size_t)228 * 1024) / (smem + 1024));
+  per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
   const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
   dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, skey, key_order, layer, D, (int)B, K, Kr,
                                                                 reservoir, top_seed, top_k, res_s, res_seed, E, count,
