@@ -188,29 +188,12 @@ def build_workload(args, world, rank, dev):
 
 @torch.no_grad()
 def run_pilot(ds, vocab, model, info, pilot_plan, n_total, args, dev):
-    """Edges and seeds from the pilot, layer group by layer group (bounded device memory)."""
-    from proteus_b200.esm import pilot
-    from proteus_b200.pilot import pilot_edges, pilot_seeds
-    L, D = info["n_layers"], info["d_ff"]
+    """Edges and seeds from the pilot on the device, a group of layers at a time (pilot_pass)."""
+    from proteus_b200.pilot import pilot_pass
     batches = list(ds.batches(vocab, None, args.tokens_per_batch, plan=pilot_plan))
-    n_tok = sum(b.valid_rows.numel() for b in batches)
-    per_layer = n_tok * D * 2
-    free = torch.cuda.mem_get_info(dev)[0]
-    group = max(1, min(L, int(0.45 * free // max(per_layer, 1))))
-    E_parts, ts_parts, rk_parts = [None] * L, [None] * L, [None] * L
-    prot = None
-    for l0 in range(0, L, group):
-        Hs, _ = pilot(model, iter(batches), dev, 1 << 62, store_device=dev, layers=range(l0, min(L, l0 + group)))
-        if prot is None:
-            prot = (pilot.last_tok // 1024).to(dev)
-        for l in range(l0, min(L, l0 + group)):
-            E = pilot_edges([Hs[l]], probs=(0.5, 0.9, 0.99, 0.999, 0.9999))
-            ts, rk = pilot_seeds([Hs[l]], E, args.K, args.Kr, n_total, groups=prot)
-            E_parts[l], ts_parts[l], rk_parts[l] = E.cpu(), ts, rk
-            Hs[l] = None
-        del Hs
-        torch.cuda.empty_cache()
-    return torch.cat(E_parts), torch.cat(ts_parts), torch.cat(rk_parts), n_tok
+    E, (ts, rk), n_tok = pilot_pass(model, batches, dev, info["n_layers"], info["d_ff"],
+                                    seeds=(args.K, args.Kr, n_total))
+    return E, ts, rk, n_tok
 
 
 def to_dev_batch(b, ctx, dev):

@@ -125,3 +125,39 @@ def pilot_seeds(Hs: list, E: torch.Tensor, K: int, Kr: int, n_total: int, c: flo
         tops.append(top)
         keys.append(key)
     return torch.stack(tops).cpu(), torch.stack(keys).cpu()
+
+
+@torch.no_grad()
+def pilot_pass(model, batches: list, device, n_layers: int, d_ff: int, probs=(0.5, 0.9, 0.99, 0.999, 0.9999),
+               seeds: tuple | None = None, edges: torch.Tensor | None = None, mem_frac: float = 0.45):
+    """Edges (and, with seeds=(K, Kr, n_total), the seeds) of a pilot over `batches`, with the pilot
+    activations kept on the device a group of layers at a time: the pilot forward runs once per
+    group, each group as large as `mem_frac` of the free device memory allows, so a large pilot
+    (C4: 660k tokens x 33 layers x 5120 units, 222 GB in bf16) never has to sit in host memory.
+    `edges` [L, 2, D, B] given: no edges are computed, only the seeds. Seeds use protein groups (the
+    sequence of each pilot row), as the reference's run_atlas does. Returns (E cpu, (top_seed,
+    res_seed_key) on the device or None, pilot token count)."""
+    from .esm import pilot
+    n_tok = sum(int(b.valid_rows.numel()) for b in batches)
+    per_layer = n_tok * d_ff * 2
+    free = torch.cuda.mem_get_info(device)[0]
+    group = max(1, min(n_layers, int(mem_frac * free // max(per_layer, 1))))
+    E_parts, ts_parts, rk_parts = [None] * n_layers, [None] * n_layers, [None] * n_layers
+    prot = None
+    for l0 in range(0, n_layers, group):
+        layers = range(l0, min(n_layers, l0 + group))
+        Hs, _ = pilot(model, iter(batches), device, 1 << 62, store_device=device, layers=layers)
+        if prot is None:
+            prot = (pilot.last_tok // 1024).to(device)
+        for l in layers:
+            El = pilot_edges([Hs[l]], probs=probs) if edges is None else edges[l:l + 1].to(device)
+            E_parts[l] = El.cpu()
+            if seeds is not None:
+                K, Kr, n_total = seeds
+                ts_parts[l], rk_parts[l] = pilot_seeds([Hs[l]], El, K, Kr, n_total, groups=prot)
+            Hs[l] = None
+        del Hs
+        torch.cuda.empty_cache()
+    E = torch.cat(E_parts)
+    sd = (torch.cat(ts_parts), torch.cat(rk_parts)) if seeds is not None else None
+    return E, sd, n_tok

@@ -28,8 +28,8 @@ import torch
 
 from .core import Atlas, AtlasConfig
 from .data import SwissProt, shuffled_order, synthetic_dataset
-from .esm import attach, flops_per_batch, load, pilot
-from .pilot import pilot_edges, pilot_seeds
+from .esm import attach, flops_per_batch, load
+from .pilot import pilot_pass
 
 
 def sync(dev):
@@ -336,24 +336,19 @@ def main(argv=None):
         E = st["atlas"]["E"]
         start = st["next_batch"]
     else:
-        if a.edges_from and not a.seed_thresholds:
+        given = None
+        if a.edges_from:
             src = torch.load(a.edges_from, map_location="cpu", weights_only=False)
-            E = src["edges"] if "edges" in src else src["atlas"]["E"]
-            Hp = None
+            given = src["edges"] if "edges" in src else src["atlas"]["E"]
+        if given is not None and not a.seed_thresholds:
+            E = given
         else:
+            # the pilot on the device, a group of layers at a time (its activations never sit in host
+            # memory), edges and seeds from the device pilot kernels
             pplan = ds.pilot_plan(plan, a.pilot_tokens, a.tokens_per_batch, a.seed)
-            Hp, _ = pilot(model, ds.batches(vocab, order, a.tokens_per_batch, plan=pplan), dev, 1 << 40)
-            if a.edges_from:
-                src = torch.load(a.edges_from, map_location="cpu", weights_only=False)
-                E = src["edges"] if "edges" in src else src["atlas"]["E"]
-            else:
-                E = torch.cat([pilot_edges([h.to(dev)], probs=tuple(a.edge_q)).cpu() for h in Hp])
-        if a.seed_thresholds:
-            prot = pilot.last_tok // 1024
-            parts = [pilot_seeds([h.to(dev)], E[li:li + 1].to(dev), a.K, a.Kr, n_total, groups=prot)
-                     for li, h in enumerate(Hp)]
-            seeds = (torch.cat([p_[0] for p_ in parts]), torch.cat([p_[1] for p_ in parts]))
-        del Hp
+            pbatches = list(ds.batches(vocab, order, a.tokens_per_batch, plan=pplan))
+            E, seeds, _ = pilot_pass(model, pbatches, torch.device(dev), L, D, probs=tuple(a.edge_q),
+                                     seeds=(a.K, a.Kr, n_total) if a.seed_thresholds else None, edges=given)
         start = a.plan_offset
     t_pilot = time.time() - t1
     atlas = Atlas(L, D, E, cfg, n_annot=len(ds.vocab) if cfg.subsample else 0, device=dev)
