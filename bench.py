@@ -881,8 +881,10 @@ def main():
                         "d2h_bytes_per_step": 32},
                 "roofline": {"kernel": "atlas_filter_compact (K1)", "bound": "hbm", "achieved": achieved,
                              "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                             "traffic": FILTER_DRAM_BYTES_PER_ROW * rows / K,
-                             "traffic_source": "ncu dram read+write of one C2 launch (16384 rows), scaled by rows",
+                             "traffic": FILTER_DRAM_BYTES_PER_ROW * valid_rows / K,
+                             "traffic_source": "ncu dram read+write of one C2 launch (16384 valid rows), scaled by "
+                                               "the valid rows per launch (the basis of achieved; padding rows are "
+                                               "read only in 32-row tiles shared with valid rows)",
                              "ms_per_launch": filt_ms, "launch_ms_quantiles": kt.quantiles_ms("filter"),
                              "launches": n_filter, "algorithmic_bytes_per_launch": bytes_launch,
                              "peak_source": peaks["source"]},
