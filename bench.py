@@ -456,7 +456,8 @@ def c2_stream(dev, peaks, scale, shift, n_blocks=64, warm=8, T=16384, D=5120):
     at.seed(ts, rk)
     seq_pos = torch.arange(T)
     blocks, ctxs = [], []
-    for b in range(n_blocks):
+    n_split = 8  # blocks after the timed ones, run again with per-kernel timers
+    for b in range(n_blocks + n_split):
         blocks.append(block())
         tok = ((seq_pos // 256) + 64 * b) * 1024 + seq_pos % 256
         ctxs.append(at.make_ctx(T, torch.arange(T), tok))  # built on the atlas's device
@@ -472,19 +473,30 @@ def c2_stream(dev, peaks, scale, shift, n_blocks=64, warm=8, T=16384, D=5120):
     torch.cuda.synchronize()
     st0 = at.stats
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("c2_stream")
     a.record()
     for i in range(warm, n_blocks):
         run(i)
     b.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     at.check_errors()
     ms = a.elapsed_time(b) / (n_blocks - warm)
     st1 = at.stats
+    # where a block's time goes: the next blocks again, with CUDA events around each kernel group
+    kt = KernelTimer()
+    at.kernel_timer = kt
+    for i in range(n_blocks, n_blocks + n_split):
+        run(i)
+    at.kernel_timer = None
+    torch.cuda.synchronize()
+    split = {k: kt.total_ms(k) / n_split for k in ("filter", "dense", "admit", "merge") if kt.count(k)}
     h_bytes = T * D * 2
     res = {"blocks_timed": n_blocks - warm, "ms_per_block": ms, "blocks_per_s": 1e3 / ms,
            "H_GBps": h_bytes / ms / 1e6, "frac_hbm_H": h_bytes / ms / 1e6 / peaks["hbm_gbs"],
            "per_block": {k: (st1[k] - st0.get(k, 0)) / (n_blocks - warm) for k in ("compacted", "top_cand", "res_cand")},
-           "dense_layer_batches": st1["dense_layer_batches"] - st0.get("dense_layer_batches", 0)}
+           "dense_layer_batches": st1["dense_layer_batches"] - st0.get("dense_layer_batches", 0),
+           "kernels_ms_per_block": split}
     del blocks, ctxs, at
     torch.cuda.empty_cache()
     return res

@@ -4,17 +4,18 @@
 //
 // 1. dense_gather: the valid rows are transposed into a column-major scratch HT [D, n_v] (coalesced
 //    reads and writes through shared-memory tiles), so every column below is one contiguous run.
-// 2. dense_column: one CTA per column, both poles.
-//    top-K: exact radix select (8-bit digits, MSB first, block-wide shared-memory histograms) of the
-//      K-th largest composite key (ordered s bits | 2^32-1-tok), i.e. the reference's top_key;
-//      digits that are constant for bf16/fp16 inputs are skipped, and token ids are read only for
-//      elements tied on the whole value. Exactly min(K, n_v) batch elements reach the threshold; the
-//      state admission tests (s > seed, key > K-th state key) then apply.
-//    reservoir: the rows in ascending hash-key order (key_order; their keys gathered once per launch
-//      into a sorted array) are split into one run per thread;
-//      each thread counts the admissible rows of its run per (pole, bin) (bin match and key under
-//      the bin's ceiling), a block scan turns the counts into global ranks, and the first Kr
-//      admissible rows of each bin are emitted. Runs that start above every ceiling stop at once.
+//    The same launch writes the rows' 32-bit hash keys in row order and in ascending key order.
+// 2. dense_column: one CTA per column at a time (grid-stride), both poles.
+//    top-K: the admissible candidates (s > seed, top_key above the state's K-th key) are counted in
+//      a row-order pass; a pole with at most K of them emits exactly those; otherwise an exact radix
+//      select (8-bit digits, MSB first, per-warp shared-memory histograms) finds the K-th largest
+//      composite key (ordered s bits | 2^32-1-tok), i.e. the reference's top_key; digits that are
+//      constant for bf16/fp16 inputs are skipped, and token ids are read only for elements tied on
+//      the whole value.
+//    reservoir: the same row-order pass counts the rows under each (pole, bin)'s key ceiling; a bin
+//      with at most Kr of them admits them all (no ordering needed), and only the bins with more
+//      walk the key order, a block-wide chunk at a time, taking their first Kr rows in ascending key
+//      order until every such bin is full or the keys pass its ceiling.
 //    Records are staged in shared memory and appended with one atomic per list per CTA.
 #include <algorithm>
 
@@ -49,13 +50,25 @@ __device__ __forceinline__ bool triggered(const int32_t* count, int64_t cap, int
 // ---------------------------------------------------------------------------------------- gather
 // Grid-stride over 32x32 tiles (tile t: rows 32*(t % nti), columns 32*(t / nti)) with a grid bounded
 // by the SM count, so the untriggered case costs a few thousand early exits, not one block per tile.
+// With key32 given, the same launch first writes the rows' 32-bit hash keys (token keys lie in
+// [0, 2^32)): key32[i] in valid-row order for the row-order passes, skey32[j] = key[key_order[j]]
+// in ascending key order for the ordered walk.
 template <typename T>
 __global__ void dense_gather_kernel(const T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
                                     int64_t n, int64_t n8, T* __restrict__ HT, int64_t ldh,
+                                    const int64_t* __restrict__ key, const int32_t* __restrict__ key_order,
+                                    uint32_t* __restrict__ key32, uint32_t* __restrict__ skey32,
                                     const int32_t* __restrict__ count, int64_t cap, int force) {
   if (!triggered(count, cap, force)) return;
   __shared__ T tile[32][33];
   const int tx = threadIdx.x, ty = threadIdx.y;
+  if (key32 != nullptr) {
+    const int64_t stride = (int64_t)gridDim.x * 256;
+    for (int64_t j = (int64_t)blockIdx.x * 256 + ty * 32 + tx; j < n; j += stride) {
+      key32[j] = (uint32_t)key[j];
+      skey32[j] = (uint32_t)key[key_order[j]];
+    }
+  }
   const int64_t nti = (n8 + 31) / 32, ntiles = nti * ((D + 31) / 32);
   for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
     const int64_t i0 = (t % nti) * 32, d0 = (t / nti) * 32;
@@ -74,48 +87,50 @@ __global__ void dense_gather_kernel(const T* __restrict__ H, int64_t D, int64_t 
   }
 }
 
-// Keys in key order (skey[j] = key[key_order[j]]), once per triggered launch: the reservoir walk of
-// every column then reads them sequentially instead of one random 8-byte load per row and column.
-__global__ void dense_sorted_keys_kernel(const int64_t* __restrict__ key, const int32_t* __restrict__ key_order,
-                                         int64_t n_v, int64_t* __restrict__ skey, const int32_t* __restrict__ count,
-                                         int64_t cap, int force) {
-  if (!triggered(count, cap, force)) return;
-  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n_v; j += (int64_t)gridDim.x * blockDim.x)
-    skey[j] = key[key_order[j]];
-}
-
 // ---------------------------------------------------------------------------------------- column
+// Records of one column staged in shared memory: top-K records from slot 0 up (at most 2K),
+// reservoir records from slot kStage-1 down (at most kStage - 2K >= 2*B*Kr); each part is appended
+// to its list with one global atomic per CTA.
 struct Staged {
   int32_t g[kStage];
   int64_t sc[kStage], tok[kStage];
   float val[kStage];
-  int n;
+  int n, m;
 };
 
-__device__ __forceinline__ void stage(Staged& st, int32_t g, int64_t sc, int64_t tok, float val, int32_t* err) {
+__device__ __forceinline__ void stage_top(Staged& st, int lim, int32_t g, int64_t sc, int64_t tok, float val,
+                                          int32_t* err) {
   const int i = atomicAdd(&st.n, 1);
-  if (i < kStage) {
+  if (i < lim) {
     st.g[i] = g; st.sc[i] = sc; st.tok[i] = tok; st.val[i] = val;
   } else {
     atomicExch(err, 1);
   }
 }
 
-__device__ void flush(Staged& st, const Lists& o, int32_t* err, int* s_base) {
-  __syncthreads();
-  const int n = st.n < kStage ? st.n : kStage;
+__device__ __forceinline__ void stage_res(Staged& st, int lim, int32_t g, int64_t sc, int64_t tok, float val,
+                                          int32_t* err) {
+  const int j = atomicAdd(&st.m, 1);
+  if (j < lim) {
+    const int i = kStage - 1 - j;
+    st.g[i] = g; st.sc[i] = sc; st.tok[i] = tok; st.val[i] = val;
+  } else {
+    atomicExch(err, 1);
+  }
+}
+
+// Appends staged slots [lo, lo + n) to list o. All threads call it after a barrier.
+__device__ void flush_range(const Staged& st, int lo, int n, const Lists& o, int32_t* err, int* s_base) {
   if (threadIdx.x == 0) *s_base = n > 0 ? atomicAdd(o.n, n) : 0;
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int64_t slot = (int64_t)*s_base + i;
     if (slot < o.cap) {
-      o.g[slot] = st.g[i]; o.sc[slot] = st.sc[i]; o.tok[slot] = st.tok[i]; o.val[slot] = st.val[i];
+      o.g[slot] = st.g[lo + i]; o.sc[slot] = st.sc[lo + i]; o.tok[slot] = st.tok[lo + i]; o.val[slot] = st.val[lo + i];
     } else {
       atomicExch(err, 1);
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) st.n = 0;
   __syncthreads();
 }
 
@@ -125,19 +140,42 @@ struct ColShared {
   unsigned long long P[2];
   int need[2], nbits[2], done[2];
   int cand[2];                            // admissible top-K candidates per pole
-  int scan[kThreads / 32][2 * kMaxB];
   int64_t ceil[2 * kMaxB];                // reservoir key ceiling per (pole, bin) of the column
-  uint16_t rcnt[2 * kMaxB][kThreads];     // per thread and (pole, bin): count, then start rank
+  int rtot[2 * kMaxB];                    // rows under the ceiling per (pole, bin) in the batch
+  int rfound[2 * kMaxB];                  // ordered walk: rows admitted so far per (pole, bin)
+  int wcnt[kThreads / 32][2 * kMaxB];     // ordered walk: per-warp counts of one chunk
   int base;
   Staged st;
 };
 
-// One column d of the layer (the CTA's threads together): top-K radix select and reservoir runs.
+// Reservoir slot (p * kMaxB + bin) of value s for pole p, or -1 below the pole's lowest edge.
+// Unused edges are NaN, so bin never exceeds B-1.
+template <int P>
+__device__ __forceinline__ int res_slot(float s, const float (&e)[2][kMaxB]) {
+  if (!(s >= e[P][0])) return -1;
+  int bin = 0;
+#pragma unroll
+  for (int b = 1; b < kMaxB; ++b) bin += (s >= e[P][b]) ? 1 : 0;
+  return P * kMaxB + bin;
+}
+
+// One column d of the layer (the CTA's threads together).
+//  pass A (row order): admissible top-K candidates per pole (s > seed, top_key above the state's
+//    K-th key) and rows under the ceiling per reservoir (pole, bin);
+//  top-K: when a pole has at most K candidates they are exactly the records to merge; otherwise an
+//    exact radix select (8-bit digits, MSB first) of the K-th largest composite key
+//    (ordered s bits | 2^32-1-tok), i.e. the reference's top_key, finds the threshold;
+//  pass B (row order): the top-K records, and every row of a reservoir bin with at most Kr rows
+//    under its ceiling (all of them are admitted, whatever their key order);
+//  ordered walk: bins with more than Kr such rows take their first Kr in ascending key order,
+//    walking the key order a block-wide chunk at a time until every such bin is full or the keys
+//    pass its ceiling (for a dense bin this ends within a few chunks).
 template <int DT>
 __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T* scol, int64_t d,
                                              const typename Elem<DT>::T* __restrict__ HT,
                                              int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
-                                             const int64_t* __restrict__ skey, const int32_t* __restrict__ key_order,
+                                             const uint32_t* __restrict__ key32, const uint32_t* __restrict__ skey32,
+                                             const int32_t* __restrict__ key_order,
                                              int64_t layer, int64_t D, int B, int64_t K, int64_t Kr, int reservoir,
                                              const float* __restrict__ top_seed, const int64_t* __restrict__ top_k,
                                              const int64_t* __restrict__ res_s, const int64_t* __restrict__ res_seed,
@@ -152,6 +190,7 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
     for (int64_t i = tid; i < nvec; i += kThreads) dst[i] = __ldcs(src + i);
     col = scol;
   }
+  const int top_lim = (int)(2 * K), res_lim = kStage - (int)(2 * K);
   int64_t kth[2];
   float seed[2];
 #pragma unroll
@@ -160,19 +199,47 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
     kth[p] = top_k[g * K + (K - 1)];
     seed[p] = top_seed[g];
   }
+  // reservoir edges in registers (NaN for unused bins: compares false, even against +inf); the key
+  // ceilings in shared memory (admit key < ceiling)
+  float e[2][kMaxB];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) {
+      e[p][b] = __int_as_float(0x7FC00000);
+      if (reservoir && b < B) e[p][b] = E[((layer * 2 + p) * D + d) * B + b];
+    }
+  }
+  if (tid < 2 * kMaxB) {
+    const int p = tid / kMaxB, b = tid % kMaxB;
+    int64_t c = 0;
+    if (reservoir && b < B) {
+      const int64_t gr = ((layer * 2 + p) * D + d) * B + b;
+      int64_t th = res_s[gr * Kr + (Kr - 1)];
+      const int64_t sd = res_seed[gr];
+      if (sd > th) th = sd;
+      c = (th == kI64Min) ? (1ll << 32) : -th;
+    }
+    sh.ceil[tid] = c;
+    sh.rtot[tid] = 0;
+    sh.rfound[tid] = 0;
+  }
   if (tid < 2) {
     sh.P[tid] = 0;
     sh.need[tid] = (int)K;
     sh.nbits[tid] = 0;
     sh.cand[tid] = 0;
   }
-  if (tid == 0) sh.st.n = 0;
+  if (tid == 0) {
+    sh.st.n = 0;
+    sh.st.m = 0;
+  }
+  for (int i = tid; i < (kThreads / 32) * 2 * kMaxB; i += kThreads) (&sh.wcnt[0][0])[i] = 0;
   __syncthreads();
-  // Admissible top-K candidates of the batch: s > seed and top_key(s, tok) above the state's K-th
-  // key (only those can enter the state). When a pole has at most K of them they are exactly the
-  // records to merge, and its radix select is skipped (the common case once the state is full).
+  // ------------------------------------------------------------------ pass A
   {
     int c0 = 0, c1 = 0;
+    uint64_t rc[2][2] = {{0ull, 0ull}, {0ull, 0ull}};  // 16-bit counts per (pole, bin): [p][bin / 4]
     const uint64_t ku0 = (uint64_t)kth[0] ^ 0x8000000000000000ull, ku1 = (uint64_t)kth[1] ^ 0x8000000000000000ull;
     for (int64_t i = tid; i < n_v; i += kThreads) {
       const float h = Elem<DT>::f(col[i]);
@@ -189,6 +256,18 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
           if (c > ku) (p ? c1 : c0)++;
         }
       }
+      if (reservoir) {
+        const int64_t k = (int64_t)key32[i];
+        const int sa = res_slot<0>(h, e), sb = res_slot<1>(-h, e);
+        if (sa >= 0 && k < sh.ceil[sa]) {
+          const uint64_t inc = 1ull << (16 * (sa & 3));
+          if (sa < 4) rc[0][0] += inc; else rc[0][1] += inc;
+        }
+        if (sb >= 0 && k < sh.ceil[sb]) {
+          const uint64_t inc = 1ull << (16 * (sb & 3));
+          if (sb < kMaxB + 4) rc[1][0] += inc; else rc[1][1] += inc;
+        }
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -198,6 +277,19 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
     if (lane == 0) {
       atomicAdd(&sh.cand[0], c0);
       atomicAdd(&sh.cand[1], c1);
+    }
+    if (reservoir) {
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+#pragma unroll
+        for (int b = 0; b < kMaxB; ++b) {
+          if (b >= B) break;
+          int v = (int)((rc[p][b >> 2] >> (16 * (b & 3))) & 0xFFFFull);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+          if (lane == 0 && v) atomicAdd(&sh.rtot[p * kMaxB + b], v);
+        }
+      }
     }
   }
   __syncthreads();
@@ -295,6 +387,17 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
     const int nb = sh.nbits[p];
     thr[p] = (nb >= 64 ? sh.P[p] : (nb == 0 ? 0ull : (sh.P[p] << (64 - nb))));
   }
+  // reservoir bins decided by pass A: at most Kr rows under the ceiling -> all admitted here
+  uint32_t direct = 0, ordered = 0;
+  if (reservoir) {
+#pragma unroll
+    for (int c = 0; c < 2 * kMaxB; ++c) {
+      const int t = sh.rtot[c];
+      if (t > 0 && t <= Kr) direct |= 1u << c;
+      if (t > Kr) ordered |= 1u << c;
+    }
+  }
+  // ------------------------------------------------------------------ pass B
   for (int64_t i = tid; i < n_v; i += kThreads) {
     const float h = Elem<DT>::f(col[i]);
 #pragma unroll
@@ -306,109 +409,88 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
       const uint64_t c = ((uint64_t)hi << 32) | (uint64_t)(kM32 - (uint32_t)t);
       if (c >= thr[p]) {
         const int64_t k64 = (int64_t)(c ^ 0x8000000000000000ull);
-        if (k64 > kth[p]) stage(sh.st, (int32_t)((layer * 2 + p) * D + d), k64, t, s, err);
+        if (k64 > kth[p]) stage_top(sh.st, top_lim, (int32_t)((layer * 2 + p) * D + d), k64, t, s, err);
+      }
+    }
+    if (direct) {
+      const int sa = res_slot<0>(h, e), sb = res_slot<1>(-h, e);
+      const bool da = sa >= 0 && ((direct >> sa) & 1u), db = sb >= 0 && ((direct >> sb) & 1u);
+      if (da || db) {
+        const int64_t k = (int64_t)key32[i];
+        if (da && k < sh.ceil[sa])
+          stage_res(sh.st, res_lim, (int32_t)(((layer * 2) * D + d) * B + sa), -k, tok[i], h, err);
+        if (db && k < sh.ceil[sb])
+          stage_res(sh.st, res_lim, (int32_t)(((layer * 2 + 1) * D + d) * B + (sb - kMaxB)), -k, tok[i], h, err);
       }
     }
   }
-  flush(sh.st, top, err, &sh.base);
-  if (!reservoir) return;
-  // ------------------------------------------------------------------ reservoir bottom-Kr
-  // Bin edges in registers; each (pole, bin) slot c = p*kMaxB + b has its key ceiling in shared
-  // memory, and each thread its count (then its start rank) per slot in shared memory, so a row
-  // costs one shared load / store for its own slot instead of a compare-and-select over all slots.
-  // A row belongs to at most the pole whose lowest edge it reaches (both only on a tie with it).
-  float e[2][kMaxB];
-  int64_t maxceil = 0;
+  // ------------------------------------------------------------------ ordered walk
+  if (ordered) {
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int64_t j0 = 0; j0 < n_v; j0 += kThreads) {
+      // the open bins and their largest ceiling (every thread reads the same shared values)
+      uint32_t open = 0;
+      int64_t maxc = 0;
 #pragma unroll
-  for (int p = 0; p < 2; ++p) {
-#pragma unroll
-    for (int b = 0; b < kMaxB; ++b) {
-      e[p][b] = __int_as_float(0x7FC00000);  // NaN: an unused edge compares false, even for +inf
-      int64_t c = 0;
-      if (b < B) {
-        const int64_t gr = ((layer * 2 + p) * D + d) * B + b;
-        e[p][b] = E[gr];
-        int64_t th = res_s[gr * Kr + (Kr - 1)];
-        const int64_t sd = res_seed[gr];
-        if (sd > th) th = sd;
-        c = (th == kI64Min) ? (1ll << 32) : -th;  // admit key < ceil
-        if (c > maxceil) maxceil = c;
-      }
-      if (tid == 0) sh.ceil[p * kMaxB + b] = c;
-    }
-  }
-  for (int c = 0; c < 2 * kMaxB; ++c) sh.rcnt[c][tid] = 0;
-  __syncthreads();
-  const int64_t run = (n_v + kThreads - 1) / kThreads;
-  const int64_t j0 = tid * run;
-  const int64_t j1 = j0 + run < n_v ? j0 + run : n_v;
-  for (int64_t j = j0; j < j1; ++j) {
-    const int64_t k = skey[j];
-    if (k >= maxceil) break;
-    const float h = Elem<DT>::f(col[key_order[j]]);
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const float s = p ? -h : h;
-      if (!(s >= e[p][0])) continue;
-      int bin = 0;
-#pragma unroll
-      for (int b = 1; b < kMaxB; ++b) bin += (s >= e[p][b]) ? 1 : 0;
-      const int c = p * kMaxB + bin;
-      if (k < sh.ceil[c]) {
-        const int n = sh.rcnt[c][tid];
-        if (n < Kr) sh.rcnt[c][tid] = (uint16_t)(n + 1);
-      }
-    }
-  }
-  // block exclusive scan of the per-thread counts, for every (pole, bin); the start ranks replace
-  // the counts in place
-  bool open = false;
-#pragma unroll
-  for (int c = 0; c < 2 * kMaxB; ++c) {
-    const int v = sh.rcnt[c][tid];
-    int incl = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    if (lane == 31) sh.scan[warp][c] = incl;
-    sh.rcnt[c][tid] = (uint16_t)(incl - v);  // within-warp start, completed below
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < 2 * kMaxB; ++c) {
-    int st = sh.rcnt[c][tid];
-    for (int w = 0; w < warp; ++w) st += sh.scan[w][c];
-    const int b = c % kMaxB;
-    open |= (b < B && st < Kr);
-    sh.rcnt[c][tid] = (uint16_t)(st < 65535 ? st : 65535);
-  }
-  if (open) {
-    for (int64_t j = j0; j < j1; ++j) {
-      const int64_t k = skey[j];
-      if (k >= maxceil) break;
-      const int32_t vi = key_order[j];
-      const float h = Elem<DT>::f(col[vi]);
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const float s = p ? -h : h;
-        if (!(s >= e[p][0])) continue;
-        int bin = 0;
-#pragma unroll
-        for (int b = 1; b < kMaxB; ++b) bin += (s >= e[p][b]) ? 1 : 0;
-        const int c = p * kMaxB + bin;
-        if (k < sh.ceil[c]) {
-          const int st = sh.rcnt[c][tid];
-          if (st < Kr) {
-            stage(sh.st, (int32_t)(((layer * 2 + p) * D + d) * B + bin), -k, tok[vi], h, err);
-            sh.rcnt[c][tid] = (uint16_t)(st + 1);
-          }
+      for (int c = 0; c < 2 * kMaxB; ++c) {
+        if (((ordered >> c) & 1u) && sh.rfound[c] < Kr) {
+          open |= 1u << c;
+          maxc = sh.ceil[c] > maxc ? sh.ceil[c] : maxc;
         }
       }
+      if (!open || (int64_t)skey32[j0] >= maxc) break;  // keys ascend: nothing further is admissible
+      const int64_t j = j0 + tid;
+      int sl[2] = {-1, -1};
+      int64_t k = 0;
+      int32_t vi = 0;
+      float h = 0.f;
+      if (j < n_v) {
+        k = (int64_t)skey32[j];
+        if (k < maxc) {
+          vi = key_order[j];
+          h = Elem<DT>::f(col[vi]);
+          const int sa = res_slot<0>(h, e), sb = res_slot<1>(-h, e);
+          if (sa >= 0 && ((open >> sa) & 1u) && k < sh.ceil[sa]) sl[0] = sa;
+          if (sb >= 0 && ((open >> sb) & 1u) && k < sh.ceil[sb]) sl[1] = sb;
+        }
+      }
+      int rk[2];
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const uint32_t peers = __match_any_sync(0xFFFFFFFFu, sl[p]);
+        rk[p] = __popc(peers & lt);
+        if (sl[p] >= 0 && rk[p] == 0) sh.wcnt[warp][sl[p]] = __popc(peers);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int c = sl[p];
+        if (c < 0) continue;
+        int off = sh.rfound[c] + rk[p];
+        for (int w = 0; w < warp; ++w) off += sh.wcnt[w][c];
+        if (off < Kr) {
+          const int bin = p ? c - kMaxB : c;
+          stage_res(sh.st, res_lim, (int32_t)(((layer * 2 + p) * D + d) * B + bin), -k, tok[vi], h, err);
+        }
+      }
+      __syncthreads();
+      if (tid < 2 * kMaxB) {
+        int t = 0;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) {
+          t += sh.wcnt[w][tid];
+          sh.wcnt[w][tid] = 0;
+        }
+        sh.rfound[tid] += t;
+      }
+      __syncthreads();
     }
   }
-  flush(sh.st, res, err, &sh.base);
+  __syncthreads();
+  const int n_top = sh.st.n < top_lim ? sh.st.n : top_lim;
+  const int n_res = sh.st.m < res_lim ? sh.st.m : res_lim;
+  flush_range(sh.st, 0, n_top, top, err, &sh.base);
+  flush_range(sh.st, kStage - n_res, n_res, res, err, &sh.base);
 }
 
 // Columns are taken grid-stride by at most one resident wave of CTAs, so an untriggered launch costs
@@ -416,7 +498,8 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 4)
 dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
-                    const int64_t* __restrict__ skey, const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
+                    const uint32_t* __restrict__ key32, const uint32_t* __restrict__ skey32,
+                    const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
                     int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
                     const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
                     const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
@@ -428,8 +511,8 @@ dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, in
   auto* scol = col_in_smem ? reinterpret_cast<typename Elem<DT>::T*>(col_raw + ((sizeof(ColShared) + 15) / 16) * 16)
                            : nullptr;
   for (int64_t d = blockIdx.x; d < D; d += gridDim.x) {
-    dense_column<DT>(sh, scol, d, HT, ldh, n_v, tok, skey, key_order, layer, D, B, K, Kr, reservoir, top_seed, top_k,
-                     res_s, res_seed, E, top, res, err);
+    dense_column<DT>(sh, scol, d, HT, ldh, n_v, tok, key32, skey32, key_order, layer, D, B, K, Kr, reservoir, top_seed,
+                     top_k, res_s, res_seed, E, top, res, err);
     __syncthreads();  // the next column re-initialises the shared state and the staged column
   }
 }
@@ -445,15 +528,14 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   T* HT = reinterpret_cast<T*>(scratch);
   const int64_t ntiles = (n8 + 31) / 32 * ((D + 31) / 32);
   const unsigned g1 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)num_sms() * 8));
+  // 32-bit keys in row order, then in key order, after the transposed copy (16-byte aligned:
+  // D * n8 * esize is a multiple of 16)
+  uint32_t* key32 = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(scratch) + D * n8 * (int64_t)sizeof(T));
+  uint32_t* skey32 = key32 + n8;
   dense_gather_kernel<T><<<g1, dim3(32, 8), 0, st>>>(reinterpret_cast<const T*>(H), D, ld, valid_rows, n_v, n8, HT, n8,
-                                                     count, cap, force);
+                                                     reservoir ? key : nullptr, key_order, reservoir ? key32 : nullptr,
+                                                     skey32, count, cap, force);
   if (int e = check_launch("atlas_dense_select: gather")) return e;
-  // sorted keys after the transposed copy (16-byte aligned: D * n8 * esize is a multiple of 16)
-  int64_t* skey = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(scratch) + D * n8 * (int64_t)sizeof(T));
-  if (reservoir) {
-    dense_sorted_keys_kernel<<<grid_for(n_v, 256, 2), 256, 0, st>>>(key, key_order, n_v, skey, count, cap, force);
-    if (int e = check_launch("atlas_dense_select: sorted keys")) return e;
-  }
   // the column goes to shared memory when it fits next to the shared state (C4: ~62 KB of bf16 per
   // column, two CTAs per SM); otherwise it is read from the transposed copy in global memory
   const size_t base_smem = ((sizeof(ColShared) + 15) / 16) * 16;
@@ -476,7 +558,7 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   int per_sm = (int)(((size_t)228 * 1024) / (smem + 1024));
   per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
   const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
-  dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, skey, key_order, layer, D, (int)B, K, Kr,
+  dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, key32, skey32, key_order, layer, D, (int)B, K, Kr,
                                                                 reservoir, top_seed, top_k, res_s, res_seed, E, count,
                                                                 cap, force, top, res, err, col_in_smem);
   return check_launch("atlas_dense_select: column");
@@ -492,7 +574,7 @@ using namespace atlas;
 extern "C" int64_t atlas_dense_scratch_bytes(int64_t n_v, int64_t D, int64_t B, int dtype) {
   (void)B;
   const int64_t n8 = (n_v + 7) / 8 * 8;
-  return D * n8 * esize(dtype) + n8 * 8 + 256;  // transposed valid rows, then the keys in key order
+  return D * n8 * esize(dtype) + n8 * 8 + 256;  // transposed valid rows, 32-bit keys in row and key order
 }
 
 extern "C" int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, int64_t layer,
@@ -509,6 +591,7 @@ extern "C" int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D
                 kMaxB);
   ATLAS_REQUIRE(2 * K + 2 * B * Kr <= kStage, "dense_select: K/Kr too large for the staging area");
   ATLAS_REQUIRE((layer * 2 + 2) * D * B < (1LL << 31) && n_v < (1LL << 31), "dense_select: ids exceed int32");
+  ATLAS_REQUIRE(n_v <= (int64_t)kThreads * 65535, "dense_select: more than %d valid rows", kThreads * 65535);
   (void)flag;
   if (n_v == 0) return ATLAS_OK;
   ATLAS_REQUIRE(force || count, "dense_select: count required unless forced");
