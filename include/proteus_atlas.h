@@ -214,8 +214,10 @@ int atlas_admit(int64_t L, int64_t D, int64_t B, int64_t K, int64_t Kr, int64_t 
  * batch elements that can enter the state's top-K) and, per bin, the Kr smallest keys among rows in
  * the bin under the bin's key ceiling; admitted records are appended to the same lists as
  * atlas_admit. key_order: valid-row indices sorted by key ascending. scratch: device bytes,
- * >= atlas_dense_scratch_bytes(n_v, D, B, dtype) (a column-major copy of the valid rows and the
- * keys in key order).
+ * >= atlas_dense_scratch_bytes(n_v, D, B, dtype) (per-column partial counts of the row ranges, the
+ * per-column decisions and hard-column lists, the keys in key order), ZERO-FILLED before its first
+ * use: the call counts arrivals in some of its words and leaves them at zero, so a buffer kept for
+ * later calls needs no further clearing.
  * `flag` is unused (kept for ABI stability); K <= 256, Kr <= 256, 2K + 2*B*Kr <= 1024.
  */
 int64_t atlas_dense_scratch_bytes(int64_t n_v, int64_t D, int64_t B, int dtype);

@@ -90,7 +90,7 @@ _KERNELS.update({"atlas_ctx_rows": 4, "atlas_ctx_annotations": 2})
 
 def _n_kernels(name: str, args) -> int:
     if name == "atlas_dense_select":
-        return 2  # valid-row gather (with the key arrays when there is a reservoir), columns
+        return 3  # row-major count (+ keys in key order), row-major emit, hard columns
     if name == "atlas_admit":  # candidates, plus the bulk-row kernel when there are bulk rows
         return 2 if (args[6] and args[20]) else 1
     if name.endswith("_bytes") or name.endswith("_i32"):

@@ -402,7 +402,8 @@ class Atlas:
         self._R_used = False
         sb = load().atlas_dense_scratch_bytes(ctx.n_v, D, B, dtype_code(self._act_dtype or torch.float32))
         if self._dense_scratch is None or self._dense_scratch.numel() < sb:
-            self._dense_scratch = torch.empty(int(sb * 1.25) + 256, dtype=torch.uint8, device=dev)
+            # zero-filled: the dense kernels count strip arrivals in it and leave those words at zero
+            self._dense_scratch = torch.zeros(int(sb * 1.25) + 256, dtype=torch.uint8, device=dev)
 
     def begin_batch(self, ctx: BatchCtx, redo_layers: list[int] | None = None):
         """Thresholds for this batch from the state at batch start (device only, no sync)."""

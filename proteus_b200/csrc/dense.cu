@@ -2,21 +2,31 @@
 // device: it runs when the layer is a dense layer (force) or when its compaction buffer overflowed
 // (*count > cap, the 0.5%-fill trigger), so the forward is never re-run and the host never syncs.
 //
-// 1. dense_gather: the valid rows are transposed into a column-major scratch HT [D, n_v] (coalesced
-//    reads and writes through shared-memory tiles), so every column below is one contiguous run.
-//    The same launch writes the rows' 32-bit hash keys in row order and in ascending key order.
-// 2. dense_column: one CTA per column at a time (grid-stride), both poles.
-//    top-K: the admissible candidates (s > seed, top_key above the state's K-th key) are counted in
-//      a row-order pass; a pole with at most K of them emits exactly those; otherwise an exact radix
-//      select (8-bit digits, MSB first, per-warp shared-memory histograms) finds the K-th largest
-//      composite key (ordered s bits | 2^32-1-tok), i.e. the reference's top_key; digits that are
-//      constant for bf16/fp16 inputs are skipped, and token ids are read only for elements tied on
-//      the whole value.
-//    reservoir: the same row-order pass counts the rows under each (pole, bin)'s key ceiling; a bin
-//      with at most Kr of them admits them all (no ordering needed), and only the bins with more
-//      walk the key order, a block-wide chunk at a time, taking their first Kr rows in ascending key
-//      order until every such bin is full or the keys pass its ceiling.
-//    Records are staged in shared memory and appended with one atomic per list per CTA.
+// Per column and pole the path selects, from the n_v valid rows, the exact top-K by top_key (the
+// only batch elements that can enter the state's top-K) and, per reservoir bin, the Kr smallest keys
+// among the rows in the bin under the bin's key ceiling. Two facts make most of that a streaming
+// pass over H:
+//  * a pole with at most K admissible candidates (s > seed and top_key above the state's K-th key)
+//    has exactly those as its records: every larger batch element is a candidate too, so each
+//    candidate lies inside the batch's top-K;
+//  * a bin with at most Kr rows under its ceiling admits all of them, for the same reason.
+// So:
+// 1. dense_count (row-major over H, one thread per column of a 256-column strip, one CTA per strip
+//    and row range): per column, the admissible top-K candidates per pole and the rows under each
+//    (pole, bin) ceiling, as per-range partial counts. The last range of a strip to finish adds the
+//    partials up and writes each column's decision: which poles need a select (> K candidates), which
+//    bins are direct (1..Kr rows) and which ordered (> Kr rows), and the strip's list of such "hard"
+//    columns. The same launch writes the rows' 32-bit keys in ascending key order.
+// 2. dense_emit (the same grid): the records of every direct pole and bin, staged per CTA in shared
+//    memory and appended with one atomic per list.
+// 3. dense_hard (one CTA per hard column at a time, grid-stride): the column staged in shared memory
+//    from H; poles that need it take an exact radix select (8-bit digits, MSB first, per-warp
+//    shared-memory histograms) of the K-th largest composite key (ordered s bits | 2^32-1-tok), i.e.
+//    the reference's top_key, then emit; ordered bins take their first Kr rows in ascending key
+//    order, walking the key order a block-wide chunk at a time until every such bin is full or the
+//    keys pass its ceiling (a dense bin ends within a few chunks).
+// Passes 1 and 2 read H once each (coalesced, 64 bytes per warp and row); pass 3 only touches the
+// hard columns, which are all columns only when the state is empty.
 #include <algorithm>
 
 #include "common.cuh"
@@ -26,12 +36,60 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxB = 8;
-constexpr int kStage = 1024;  // staged records per CTA (top: <= 2K; reservoir: <= 2*B*Kr)
-constexpr int kDenseSmemMax = 227 * 1024;  // opt-in shared memory per CTA
+constexpr int kSlots = 2 * kMaxB;         // reservoir (pole, bin) slots: p * kMaxB + bin
+constexpr int kStage = 1024;              // staged records per hard-column CTA (top: <= 2K; reservoir: <= 2*B*Kr)
+constexpr int kEmitHalf = 256;            // staged records per emit CTA and list (overflow goes straight out)
+constexpr int kStrip = 256;               // columns per strip: one per thread of the count and emit kernels
+constexpr int kRangesMax = 64;            // row ranges per strip
+constexpr int kPartRows = 2 + kSlots;     // partial counts per (range, column): 2 poles + 16 slots
+constexpr int kU = 4;                     // rows in flight per thread in the row-major kernels
+constexpr int kDenseSmemMax = 227 * 1024; // opt-in shared memory per CTA
 
 struct Lists {
   int32_t* g; int64_t* sc; int64_t* tok; float* val; int32_t* n; int64_t cap;
 };
+
+// Scratch of one call, carved from the caller's buffer (zero-filled before its first use; the
+// ticket words are left at zero by every call).
+struct DenseWs {
+  int32_t* part;     // [R][kPartRows][D] partial counts of the row ranges
+  uint32_t* dec;     // [D] reservoir decisions: bits 0-15 direct slots, 16-31 ordered slots
+  uint32_t* tdec;    // [D] top-K decisions: bit p set when pole p needs the radix select
+  int32_t* hard;     // [strips][kStrip] hard columns of each strip
+  int32_t* nhard;    // [strips]
+  int32_t* ticket;   // [strips] ranges of the strip done counting
+  uint32_t* skey32;  // [n8] keys in ascending key order
+};
+
+int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+__host__ __device__ inline int64_t n_strips(int64_t D) { return (D + kStrip - 1) / kStrip; }
+
+int64_t ws_bytes(int64_t n_v, int64_t D) {
+  const int64_t S = n_strips(D), n8 = (n_v + 7) / 8 * 8;
+  return 256 + align256((int64_t)kRangesMax * kPartRows * D * 4) + 2 * align256(D * 4) + align256(S * kStrip * 4) +
+         2 * align256(S * 4) + align256(n8 * 4);
+}
+
+DenseWs carve(void* scratch, int64_t n_v, int64_t D) {
+  const int64_t S = n_strips(D), n8 = (n_v + 7) / 8 * 8;
+  uint8_t* p = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(scratch) + 255) & ~uintptr_t(255));
+  DenseWs w;
+  w.part = reinterpret_cast<int32_t*>(p);
+  p += align256((int64_t)kRangesMax * kPartRows * D * 4);
+  w.dec = reinterpret_cast<uint32_t*>(p);
+  p += align256(D * 4);
+  w.tdec = reinterpret_cast<uint32_t*>(p);
+  p += align256(D * 4);
+  w.hard = reinterpret_cast<int32_t*>(p);
+  p += align256(S * kStrip * 4);
+  w.nhard = reinterpret_cast<int32_t*>(p);
+  p += align256(S * 4);
+  w.ticket = reinterpret_cast<int32_t*>(p);
+  p += align256(S * 4);
+  w.skey32 = reinterpret_cast<uint32_t*>(p);
+  (void)n8;
+  return w;
+}
 
 // High word of the composite key (ordered s bits, unsigned order): top_key's value part.
 __device__ __forceinline__ uint32_t key_hi(float s) { return (uint32_t)(int32_t)ordered_f32(s) ^ 0x80000000u; }
@@ -47,48 +105,300 @@ __device__ __forceinline__ bool triggered(const int32_t* count, int64_t cap, int
   return force || (int64_t)*count > cap;
 }
 
-// ---------------------------------------------------------------------------------------- gather
-// Grid-stride over 32x32 tiles (tile t: rows 32*(t % nti), columns 32*(t / nti)) with a grid bounded
-// by the SM count, so the untriggered case costs a few thousand early exits, not one block per tile.
-// With key32 given, the same launch first writes the rows' 32-bit hash keys (token keys lie in
-// [0, 2^32)): key32[i] in valid-row order for the row-order passes, skey32[j] = key[key_order[j]]
-// in ascending key order for the ordered walk.
-template <typename T>
-__global__ void dense_gather_kernel(const T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
-                                    int64_t n, int64_t n8, T* __restrict__ HT, int64_t ldh,
-                                    const int64_t* __restrict__ key, const int32_t* __restrict__ key_order,
-                                    uint32_t* __restrict__ key32, uint32_t* __restrict__ skey32,
-                                    const int32_t* __restrict__ count, int64_t cap, int force) {
-  if (!triggered(count, cap, force)) return;
-  __shared__ T tile[32][33];
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  if (key32 != nullptr) {
-    const int64_t stride = (int64_t)gridDim.x * 256;
-    for (int64_t j = (int64_t)blockIdx.x * 256 + ty * 32 + tx; j < n; j += stride) {
-      key32[j] = (uint32_t)key[j];
-      skey32[j] = (uint32_t)key[key_order[j]];
-    }
-  }
-  const int64_t nti = (n8 + 31) / 32, ntiles = nti * ((D + 31) / 32);
-  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-    const int64_t i0 = (t % nti) * 32, d0 = (t / nti) * 32;
-    for (int k = ty; k < 32; k += 8) {
-      const int64_t i = i0 + k, d = d0 + tx;
-      T v = T(0.0f);
-      if (i < n && d < D) v = H[(int64_t)rows[i] * ld + d];
-      tile[k][tx] = v;
-    }
-    __syncthreads();
-    for (int k = ty; k < 32; k += 8) {
-      const int64_t d = d0 + k, i = i0 + tx;
-      if (d < D && i < n8) HT[d * ldh + i] = tile[tx][k];
-    }
-    __syncthreads();
+// Per-column parameters of the state: the top-K seed and K-th state key per pole, the reservoir
+// edges (NaN for unused bins: compares false, even against +inf) and the key ceilings per slot
+// (admit key < ceiling).
+struct ColParams {
+  float seed[2];
+  uint64_t ku[2];  // the state's K-th key in unsigned order (top_key ^ sign bit)
+  float e[2][kMaxB];
+};
+
+__device__ __forceinline__ void load_params(ColParams& cp, bool ok, int64_t layer, int64_t D, int64_t d, int B,
+                                            int64_t K, int reservoir, const float* __restrict__ top_seed,
+                                            const int64_t* __restrict__ top_k, const float* __restrict__ E) {
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int64_t g = (layer * 2 + p) * D + d;
+    cp.seed[p] = ok ? top_seed[g] : __int_as_float(0x7F800000);  // +inf: no candidate
+    cp.ku[p] = (uint64_t)(ok ? top_k[g * K + (K - 1)] : 0) ^ 0x8000000000000000ull;
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b)
+      cp.e[p][b] = (ok && reservoir && b < B) ? E[g * B + b] : __int_as_float(0x7FC00000);
   }
 }
 
-// ---------------------------------------------------------------------------------------- column
-// Records of one column staged in shared memory: top-K records from slot 0 up (at most 2K),
+__device__ __forceinline__ int64_t slot_ceiling(int slot, bool ok, int64_t layer, int64_t D, int64_t d, int B,
+                                                int64_t Kr, int reservoir, const int64_t* __restrict__ res_s,
+                                                const int64_t* __restrict__ res_seed) {
+  const int p = slot / kMaxB, b = slot % kMaxB;
+  if (!ok || !reservoir || b >= B) return 0;
+  const int64_t gr = ((layer * 2 + p) * D + d) * B + b;
+  int64_t th = res_s[gr * Kr + (Kr - 1)];
+  const int64_t sd = res_seed[gr];
+  if (sd > th) th = sd;
+  return (th == kI64Min) ? (1ll << 32) : -th;
+}
+
+// Admissible top-K candidate: s > seed and top_key(s, tok) above the state's K-th key (token ids are
+// read only on a tie of the value part).
+__device__ __forceinline__ bool top_candidate(float s, float seed, uint64_t ku, const int64_t* __restrict__ tok,
+                                              int64_t i) {
+  if (!(s > seed)) return false;
+  const uint32_t hi = key_hi(s), khi = (uint32_t)(ku >> 32);
+  if (hi != khi) return hi > khi;
+  const uint64_t c = ((uint64_t)hi << 32) | (uint64_t)(kM32 - (uint32_t)tok[i]);
+  return c > ku;
+}
+
+// Reservoir slot (p * kMaxB + bin) of value s for pole P, or -1 below the pole's lowest edge.
+template <int P>
+__device__ __forceinline__ int res_slot(float s, const float (&e)[2][kMaxB]) {
+  if (!(s >= e[P][0])) return -1;
+  int bin = 0;
+#pragma unroll
+  for (int b = 1; b < kMaxB; ++b) bin += (s >= e[P][b]) ? 1 : 0;
+  return P * kMaxB + bin;
+}
+
+// Row range r of R over n_v rows.
+__device__ __forceinline__ void row_range(int64_t n_v, int r, int R, int64_t& i0, int64_t& i1) {
+  i0 = n_v * r / R;
+  i1 = n_v * (r + 1) / R;
+}
+
+// ------------------------------------------------------------------------------------ 1. count
+template <int DT>
+__global__ void __launch_bounds__(kStrip, 4)
+dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
+                   int64_t n_v, const int64_t* __restrict__ tok, const int64_t* __restrict__ key,
+                   const int32_t* __restrict__ key_order, int64_t layer, int B, int64_t K, int64_t Kr, int reservoir,
+                   const float* __restrict__ top_seed, const int64_t* __restrict__ top_k,
+                   const int64_t* __restrict__ res_s, const int64_t* __restrict__ res_seed, const float* __restrict__ E,
+                   const int32_t* __restrict__ count, int64_t cap, int force, DenseWs ws) {
+  using T = typename Elem<DT>::T;
+  if (!triggered(count, cap, force)) return;
+  __shared__ int64_t s_ceil[kSlots][kStrip];
+  __shared__ int s_wn[kThreads / 32];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int strip = blockIdx.x, r = blockIdx.y, R = gridDim.y;
+  const int64_t d = (int64_t)strip * kStrip + tid;
+  const bool ok = d < D;
+  if (reservoir) {  // the keys in ascending key order, for the hard columns' ordered walks
+    const int64_t nth = (int64_t)gridDim.x * gridDim.y * kThreads;
+    for (int64_t j = ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * kThreads + tid; j < n_v; j += nth)
+      ws.skey32[j] = (uint32_t)key[key_order[j]];
+  }
+  ColParams cp;
+  load_params(cp, ok, layer, D, d, B, K, reservoir, top_seed, top_k, E);
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) s_ceil[s][tid] = slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed);
+  int64_t i0, i1;
+  row_range(n_v, r, R, i0, i1);
+  int c0 = 0, c1 = 0;
+  uint64_t rc[2][2] = {{0ull, 0ull}, {0ull, 0ull}};  // 16-bit counts per (pole, bin): [p][bin / 4]
+  const T* Hc = H + (ok ? d : 0);
+  for (int64_t i = i0; i < i1; i += kU) {
+    T x[kU];
+    int64_t kk[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t ii = i + u < i1 ? i + u : i1 - 1;  // past the range: a repeat of the last row, not counted
+      x[u] = Hc[(int64_t)rows[ii] * ld];
+      kk[u] = reservoir ? key[ii] : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (i + u >= i1) break;
+      const float h = Elem<DT>::f(x[u]);
+      c0 += top_candidate(h, cp.seed[0], cp.ku[0], tok, i + u) ? 1 : 0;
+      c1 += top_candidate(-h, cp.seed[1], cp.ku[1], tok, i + u) ? 1 : 0;
+      if (reservoir) {
+        const int sa = res_slot<0>(h, cp.e), sb = res_slot<1>(-h, cp.e);
+        if (sa >= 0 && kk[u] < s_ceil[sa][tid]) {
+          const uint64_t inc = 1ull << (16 * (sa & 3));
+          if (sa < 4) rc[0][0] += inc; else rc[0][1] += inc;
+        }
+        if (sb >= 0 && kk[u] < s_ceil[sb][tid]) {
+          const uint64_t inc = 1ull << (16 * (sb & 3));
+          if (sb < kMaxB + 4) rc[1][0] += inc; else rc[1][1] += inc;
+        }
+      }
+    }
+  }
+  if (ok) {
+    int32_t* P = ws.part + (int64_t)r * kPartRows * D + d;
+    P[0] = c0;
+    P[D] = c1;
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s)
+      P[(int64_t)(2 + s) * D] = (int)((rc[s / kMaxB][(s % kMaxB) >> 2] >> (16 * (s & 3))) & 0xFFFFull);
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(ws.ticket + strip, 1) == R - 1) ? 1 : 0;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // the strip's last range: totals and decisions per column, then the strip's hard columns
+  uint32_t hardf = 0;
+  if (ok) {
+    int tt[kPartRows];
+#pragma unroll
+    for (int q = 0; q < kPartRows; ++q) tt[q] = 0;
+    for (int q = 0; q < R; ++q) {
+      const int32_t* P = ws.part + (int64_t)q * kPartRows * D + d;
+#pragma unroll
+      for (int k = 0; k < kPartRows; ++k) tt[k] += __ldcg(P + (int64_t)k * D);
+    }
+    uint32_t direct = 0, ordered = 0, th = 0;
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      const int t = tt[2 + s];
+      if (t > 0 && t <= Kr) direct |= 1u << s;
+      if (t > Kr) ordered |= 1u << s;
+    }
+    if (tt[0] > K) th |= 1u;
+    if (tt[1] > K) th |= 2u;
+    ws.dec[d] = direct | (ordered << 16);
+    ws.tdec[d] = th;
+    hardf = (th | ordered) ? 1u : 0u;
+  }
+  const uint32_t bal = __ballot_sync(0xFFFFFFFFu, hardf != 0);
+  if (lane == 0) s_wn[warp] = __popc(bal);
+  __syncthreads();
+  int off = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) {
+    off += w < warp ? s_wn[w] : 0;
+    tot += s_wn[w];
+  }
+  if (hardf) ws.hard[strip * kStrip + off + __popc(bal & ((1u << lane) - 1u))] = (int32_t)d;
+  if (tid == 0) {
+    ws.nhard[strip] = tot;
+    ws.ticket[strip] = 0;  // ready for the next call
+  }
+}
+
+// ------------------------------------------------------------------------------------- 2. emit
+struct EmitStage {
+  int32_t g[2][kEmitHalf];
+  int64_t sc[2][kEmitHalf], tok[2][kEmitHalf];
+  float val[2][kEmitHalf];
+  int n[2];
+  int base[2];
+};
+
+// One record of list w (0 top, 1 reservoir): a staging slot while the half has room, else straight
+// to the list (one global atomic; the list count stays exact past its capacity).
+__device__ __forceinline__ void emit_rec(EmitStage& es, int w, const Lists& o, int32_t g, int64_t sc, int64_t tk,
+                                         float v, int32_t* err) {
+  const int i = atomicAdd(&es.n[w], 1);
+  if (i < kEmitHalf) {
+    es.g[w][i] = g; es.sc[w][i] = sc; es.tok[w][i] = tk; es.val[w][i] = v;
+  } else {
+    const int64_t slot = atomicAdd(o.n, 1);
+    if (slot < o.cap) {
+      o.g[slot] = g; o.sc[slot] = sc; o.tok[slot] = tk; o.val[slot] = v;
+    } else {
+      atomicExch(err, 1);
+    }
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kStrip, 4)
+dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
+                  int64_t n_v, const int64_t* __restrict__ tok, const int64_t* __restrict__ key, int64_t layer, int B,
+                  int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
+                  const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
+                  const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
+                  int64_t cap, int force, DenseWs ws, Lists top, Lists res, int32_t* __restrict__ err) {
+  using T = typename Elem<DT>::T;
+  if (!triggered(count, cap, force)) return;
+  __shared__ int64_t s_ceil[kSlots][kStrip];
+  __shared__ EmitStage es;
+  const int tid = threadIdx.x;
+  const int strip = blockIdx.x, r = blockIdx.y, R = gridDim.y;
+  const int64_t d = (int64_t)strip * kStrip + tid;
+  const bool ok = d < D;
+  const uint32_t th = ok ? ws.tdec[d] : 3u;
+  const uint32_t direct = ok ? (ws.dec[d] & 0xFFFFu) : 0u;
+  ColParams cp;
+  load_params(cp, ok, layer, D, d, B, K, reservoir, top_seed, top_k, E);
+  if (th & 1u) cp.seed[0] = __int_as_float(0x7F800000);  // pole emitted by the hard-column kernel
+  if (th & 2u) cp.seed[1] = __int_as_float(0x7F800000);
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s)
+    s_ceil[s][tid] = ((direct >> s) & 1u) ? slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed) : 0;
+  if (tid < 2) es.n[tid] = 0;
+  __syncthreads();
+  const bool any = __syncthreads_or(ok && (((th & 3u) != 3u) || direct != 0)) != 0;
+  if (any) {
+    int64_t i0, i1;
+    row_range(n_v, r, R, i0, i1);
+    const T* Hc = H + (ok ? d : 0);
+    const int32_t g0 = (int32_t)((layer * 2) * D + d), g1 = (int32_t)((layer * 2 + 1) * D + d);
+    for (int64_t i = i0; i < i1; i += kU) {
+      T x[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t ii = i + u < i1 ? i + u : i1 - 1;
+        x[u] = Hc[(int64_t)rows[ii] * ld];
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (i + u >= i1) break;
+        const int64_t ii = i + u;
+        const float h = Elem<DT>::f(x[u]);
+        if (top_candidate(h, cp.seed[0], cp.ku[0], tok, ii)) {
+          const int64_t t = tok[ii];
+          const int64_t k64 = (int64_t)((((uint64_t)key_hi(h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
+                                        0x8000000000000000ull);
+          emit_rec(es, 0, top, g0, k64, t, h, err);
+        }
+        if (top_candidate(-h, cp.seed[1], cp.ku[1], tok, ii)) {
+          const int64_t t = tok[ii];
+          const int64_t k64 = (int64_t)((((uint64_t)key_hi(-h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
+                                        0x8000000000000000ull);
+          emit_rec(es, 0, top, g1, k64, t, -h, err);
+        }
+        if (direct) {
+          const int sa = res_slot<0>(h, cp.e), sb = res_slot<1>(-h, cp.e);
+          const bool da = sa >= 0 && ((direct >> sa) & 1u), db = sb >= 0 && ((direct >> sb) & 1u);
+          if (da || db) {
+            const int64_t k = (int64_t)(uint32_t)key[ii];
+            if (da && k < s_ceil[sa][tid]) emit_rec(es, 1, res, g0 * B + sa, -k, tok[ii], h, err);
+            if (db && k < s_ceil[sb][tid]) emit_rec(es, 1, res, g1 * B + (sb - kMaxB), -k, tok[ii], h, err);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < 2) {
+    const int n = es.n[tid] < kEmitHalf ? es.n[tid] : kEmitHalf;
+    es.base[tid] = n > 0 ? atomicAdd(tid ? res.n : top.n, n) : 0;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const Lists& o = w ? res : top;
+    const int n = es.n[w] < kEmitHalf ? es.n[w] : kEmitHalf;
+    for (int i = tid; i < n; i += kThreads) {
+      const int64_t slot = (int64_t)es.base[w] + i;
+      if (slot < o.cap) {
+        o.g[slot] = es.g[w][i]; o.sc[slot] = es.sc[w][i]; o.tok[slot] = es.tok[w][i]; o.val[slot] = es.val[w][i];
+      } else {
+        atomicExch(err, 1);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------- 3. hard columns
+// Records of one hard column staged in shared memory: top-K records from slot 0 up (at most 2K),
 // reservoir records from slot kStage-1 down (at most kStage - 2K >= 2*B*Kr); each part is appended
 // to its list with one global atomic per CTA.
 struct Staged {
@@ -139,165 +449,53 @@ struct ColShared {
   uint32_t hist[2][256];                  // their sum
   unsigned long long P[2];
   int need[2], nbits[2], done[2];
-  int cand[2];                            // admissible top-K candidates per pole
-  int64_t ceil[2 * kMaxB];                // reservoir key ceiling per (pole, bin) of the column
-  int rtot[2 * kMaxB];                    // rows under the ceiling per (pole, bin) in the batch
-  int rfound[2 * kMaxB];                  // ordered walk: rows admitted so far per (pole, bin)
-  int wcnt[kThreads / 32][2 * kMaxB];     // ordered walk: per-warp counts of one chunk
+  int64_t ceil[kSlots];                   // reservoir key ceiling per (pole, bin) of the column
+  int rfound[kSlots];                     // ordered walk: rows admitted so far per (pole, bin)
+  int wcnt[kThreads / 32][kSlots];        // ordered walk: per-warp counts of one chunk
+  int pre[kRangesMax * 4 + 1];            // hard-list prefix over the strips
   int base;
   Staged st;
 };
 
-// Reservoir slot (p * kMaxB + bin) of value s for pole p, or -1 below the pole's lowest edge.
-// Unused edges are NaN, so bin never exceeds B-1.
-template <int P>
-__device__ __forceinline__ int res_slot(float s, const float (&e)[2][kMaxB]) {
-  if (!(s >= e[P][0])) return -1;
-  int bin = 0;
-#pragma unroll
-  for (int b = 1; b < kMaxB; ++b) bin += (s >= e[P][b]) ? 1 : 0;
-  return P * kMaxB + bin;
-}
-
-// One column d of the layer (the CTA's threads together).
-//  pass A (row order): admissible top-K candidates per pole (s > seed, top_key above the state's
-//    K-th key) and rows under the ceiling per reservoir (pole, bin);
-//  top-K: when a pole has at most K candidates they are exactly the records to merge; otherwise an
-//    exact radix select (8-bit digits, MSB first) of the K-th largest composite key
-//    (ordered s bits | 2^32-1-tok), i.e. the reference's top_key, finds the threshold;
-//  pass B (row order): the top-K records, and every row of a reservoir bin with at most Kr rows
-//    under its ceiling (all of them are admitted, whatever their key order);
-//  ordered walk: bins with more than Kr such rows take their first Kr in ascending key order,
-//    walking the key order a block-wide chunk at a time until every such bin is full or the keys
-//    pass its ceiling (for a dense bin this ends within a few chunks).
+// One hard column d (the CTA's threads together): the poles flagged in th take the radix select and
+// emit their top-K records; the slots flagged in `ordered` take their first Kr rows in key order.
 template <int DT>
-__device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T* scol, int64_t d,
-                                             const typename Elem<DT>::T* __restrict__ HT,
-                                             int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
-                                             const uint32_t* __restrict__ key32, const uint32_t* __restrict__ skey32,
-                                             const int32_t* __restrict__ key_order,
-                                             int64_t layer, int64_t D, int B, int64_t K, int64_t Kr, int reservoir,
-                                             const float* __restrict__ top_seed, const int64_t* __restrict__ top_k,
-                                             const int64_t* __restrict__ res_s, const int64_t* __restrict__ res_seed,
-                                             const float* __restrict__ E, Lists top, Lists res, int32_t* __restrict__ err) {
+__device__ __forceinline__ void hard_column(ColShared& sh, typename Elem<DT>::T* scol, int64_t d,
+                                            const typename Elem<DT>::T* __restrict__ H, int64_t ld,
+                                            const int32_t* __restrict__ rows, int64_t n_v,
+                                            const int64_t* __restrict__ tok, const uint32_t* __restrict__ skey32,
+                                            const int32_t* __restrict__ key_order, int64_t layer, int64_t D, int B,
+                                            int64_t K, int64_t Kr, const float* __restrict__ top_seed,
+                                            const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
+                                            const int64_t* __restrict__ res_seed, const float* __restrict__ E,
+                                            uint32_t th, uint32_t ordered, Lists top, Lists res,
+                                            int32_t* __restrict__ err) {
   using T = typename Elem<DT>::T;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const T* col = HT + d * ldh;
-  if (scol != nullptr) {  // the whole column in shared memory: every pass below reads it from there
-    const int64_t nvec = (ldh * (int64_t)sizeof(T)) / 16;
-    const uint4* src = reinterpret_cast<const uint4*>(col);
-    uint4* dst = reinterpret_cast<uint4*>(scol);
-    for (int64_t i = tid; i < nvec; i += kThreads) dst[i] = __ldcs(src + i);
-    col = scol;
-  }
+  if (scol != nullptr)  // the column staged in shared memory: every pass below reads it from there
+    for (int64_t i = tid; i < n_v; i += kThreads) scol[i] = H[(int64_t)rows[i] * ld + d];
+  auto colv = [&](int64_t i) -> float { return Elem<DT>::f(scol ? scol[i] : H[(int64_t)rows[i] * ld + d]); };
   const int top_lim = (int)(2 * K), res_lim = kStage - (int)(2 * K);
-  int64_t kth[2];
-  float seed[2];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const int64_t g = (layer * 2 + p) * D + d;
-    kth[p] = top_k[g * K + (K - 1)];
-    seed[p] = top_seed[g];
-  }
-  // reservoir edges in registers (NaN for unused bins: compares false, even against +inf); the key
-  // ceilings in shared memory (admit key < ceiling)
-  float e[2][kMaxB];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-#pragma unroll
-    for (int b = 0; b < kMaxB; ++b) {
-      e[p][b] = __int_as_float(0x7FC00000);
-      if (reservoir && b < B) e[p][b] = E[((layer * 2 + p) * D + d) * B + b];
-    }
-  }
-  if (tid < 2 * kMaxB) {
-    const int p = tid / kMaxB, b = tid % kMaxB;
-    int64_t c = 0;
-    if (reservoir && b < B) {
-      const int64_t gr = ((layer * 2 + p) * D + d) * B + b;
-      int64_t th = res_s[gr * Kr + (Kr - 1)];
-      const int64_t sd = res_seed[gr];
-      if (sd > th) th = sd;
-      c = (th == kI64Min) ? (1ll << 32) : -th;
-    }
-    sh.ceil[tid] = c;
-    sh.rtot[tid] = 0;
+  ColParams cp;
+  load_params(cp, true, layer, D, d, B, K, ordered != 0, top_seed, top_k, E);
+  if (tid < kSlots) {
+    sh.ceil[tid] = ((ordered >> tid) & 1u) ? slot_ceiling(tid, true, layer, D, d, B, Kr, 1, res_s, res_seed) : 0;
     sh.rfound[tid] = 0;
   }
   if (tid < 2) {
     sh.P[tid] = 0;
     sh.need[tid] = (int)K;
     sh.nbits[tid] = 0;
-    sh.cand[tid] = 0;
+    sh.done[tid] = ((th >> tid) & 1u) ? 0 : 1;
   }
   if (tid == 0) {
     sh.st.n = 0;
     sh.st.m = 0;
   }
-  for (int i = tid; i < (kThreads / 32) * 2 * kMaxB; i += kThreads) (&sh.wcnt[0][0])[i] = 0;
+  for (int i = tid; i < (kThreads / 32) * kSlots; i += kThreads) (&sh.wcnt[0][0])[i] = 0;
   __syncthreads();
-  // ------------------------------------------------------------------ pass A
-  {
-    int c0 = 0, c1 = 0;
-    uint64_t rc[2][2] = {{0ull, 0ull}, {0ull, 0ull}};  // 16-bit counts per (pole, bin): [p][bin / 4]
-    const uint64_t ku0 = (uint64_t)kth[0] ^ 0x8000000000000000ull, ku1 = (uint64_t)kth[1] ^ 0x8000000000000000ull;
-    for (int64_t i = tid; i < n_v; i += kThreads) {
-      const float h = Elem<DT>::f(col[i]);
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const float s = p ? -h : h;
-        if (!(s > seed[p])) continue;
-        const uint64_t ku = p ? ku1 : ku0;
-        const uint32_t hi = key_hi(s);
-        if (hi > (uint32_t)(ku >> 32)) {
-          (p ? c1 : c0)++;
-        } else if (hi == (uint32_t)(ku >> 32)) {
-          const uint64_t c = ((uint64_t)hi << 32) | (uint64_t)(kM32 - (uint32_t)tok[i]);
-          if (c > ku) (p ? c1 : c0)++;
-        }
-      }
-      if (reservoir) {
-        const int64_t k = (int64_t)key32[i];
-        const int sa = res_slot<0>(h, e), sb = res_slot<1>(-h, e);
-        if (sa >= 0 && k < sh.ceil[sa]) {
-          const uint64_t inc = 1ull << (16 * (sa & 3));
-          if (sa < 4) rc[0][0] += inc; else rc[0][1] += inc;
-        }
-        if (sb >= 0 && k < sh.ceil[sb]) {
-          const uint64_t inc = 1ull << (16 * (sb & 3));
-          if (sb < kMaxB + 4) rc[1][0] += inc; else rc[1][1] += inc;
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      c0 += __shfl_xor_sync(0xFFFFFFFFu, c0, o);
-      c1 += __shfl_xor_sync(0xFFFFFFFFu, c1, o);
-    }
-    if (lane == 0) {
-      atomicAdd(&sh.cand[0], c0);
-      atomicAdd(&sh.cand[1], c1);
-    }
-    if (reservoir) {
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-#pragma unroll
-        for (int b = 0; b < kMaxB; ++b) {
-          if (b >= B) break;
-          int v = (int)((rc[p][b >> 2] >> (16 * (b & 3))) & 0xFFFFull);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-          if (lane == 0 && v) atomicAdd(&sh.rtot[p * kMaxB + b], v);
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (tid < 2) sh.done[tid] = (n_v <= K || sh.cand[tid] <= K) ? 1 : 0;
-  __syncthreads();
-  const bool select_all = sh.done[0] && sh.done[1];
   // ------------------------------------------------------------------ top-K radix select
-  if (!select_all) {
+  if (th) {
     for (int pass = 0; pass < 8; ++pass) {
       if (sh.done[0] && sh.done[1]) break;
       if (skip_pass<DT>(pass)) {
@@ -321,7 +519,7 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
       // value digits (passes 0-3) need only the high word of the key; token ids are read only
       // for the elements still tied on the whole value (passes 4-7)
       for (int64_t i = tid; i < n_v; i += kThreads) {
-        const float h = Elem<DT>::f(col[i]);
+        const float h = colv(i);
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           if (p == 0 ? !act0 : !act1) continue;
@@ -380,47 +578,25 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
       }
       __syncthreads();
     }
-  }
-  unsigned long long thr[2];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const int nb = sh.nbits[p];
-    thr[p] = (nb >= 64 ? sh.P[p] : (nb == 0 ? 0ull : (sh.P[p] << (64 - nb))));
-  }
-  // reservoir bins decided by pass A: at most Kr rows under the ceiling -> all admitted here
-  uint32_t direct = 0, ordered = 0;
-  if (reservoir) {
-#pragma unroll
-    for (int c = 0; c < 2 * kMaxB; ++c) {
-      const int t = sh.rtot[c];
-      if (t > 0 && t <= Kr) direct |= 1u << c;
-      if (t > Kr) ordered |= 1u << c;
-    }
-  }
-  // ------------------------------------------------------------------ pass B
-  for (int64_t i = tid; i < n_v; i += kThreads) {
-    const float h = Elem<DT>::f(col[i]);
+    unsigned long long thr[2];
 #pragma unroll
     for (int p = 0; p < 2; ++p) {
-      const float s = p ? -h : h;
-      const uint32_t hi = key_hi(s);
-      if (hi < (uint32_t)(thr[p] >> 32) || !(s > seed[p])) continue;  // below the K-th value
-      const int64_t t = tok[i];
-      const uint64_t c = ((uint64_t)hi << 32) | (uint64_t)(kM32 - (uint32_t)t);
-      if (c >= thr[p]) {
-        const int64_t k64 = (int64_t)(c ^ 0x8000000000000000ull);
-        if (k64 > kth[p]) stage_top(sh.st, top_lim, (int32_t)((layer * 2 + p) * D + d), k64, t, s, err);
-      }
+      const int nb = sh.nbits[p];
+      thr[p] = (nb >= 64 ? sh.P[p] : (nb == 0 ? 0ull : (sh.P[p] << (64 - nb))));
     }
-    if (direct) {
-      const int sa = res_slot<0>(h, e), sb = res_slot<1>(-h, e);
-      const bool da = sa >= 0 && ((direct >> sa) & 1u), db = sb >= 0 && ((direct >> sb) & 1u);
-      if (da || db) {
-        const int64_t k = (int64_t)key32[i];
-        if (da && k < sh.ceil[sa])
-          stage_res(sh.st, res_lim, (int32_t)(((layer * 2) * D + d) * B + sa), -k, tok[i], h, err);
-        if (db && k < sh.ceil[sb])
-          stage_res(sh.st, res_lim, (int32_t)(((layer * 2 + 1) * D + d) * B + (sb - kMaxB)), -k, tok[i], h, err);
+    for (int64_t i = tid; i < n_v; i += kThreads) {
+      const float h = colv(i);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        if (!((th >> p) & 1u)) continue;
+        const float s = p ? -h : h;
+        const uint32_t hi = key_hi(s);
+        if (hi < (uint32_t)(thr[p] >> 32) || !(s > cp.seed[p])) continue;  // below the K-th value
+        const int64_t t = tok[i];
+        const uint64_t c = ((uint64_t)hi << 32) | (uint64_t)(kM32 - (uint32_t)t);
+        if (c >= thr[p] && c > cp.ku[p])
+          stage_top(sh.st, top_lim, (int32_t)((layer * 2 + p) * D + d), (int64_t)(c ^ 0x8000000000000000ull), t, s,
+                    err);
       }
     }
   }
@@ -428,11 +604,11 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
   if (ordered) {
     const uint32_t lt = (1u << lane) - 1u;
     for (int64_t j0 = 0; j0 < n_v; j0 += kThreads) {
-      // the open bins and their largest ceiling (every thread reads the same shared values)
+      // the open slots and their largest ceiling (every thread reads the same shared values)
       uint32_t open = 0;
       int64_t maxc = 0;
 #pragma unroll
-      for (int c = 0; c < 2 * kMaxB; ++c) {
+      for (int c = 0; c < kSlots; ++c) {
         if (((ordered >> c) & 1u) && sh.rfound[c] < Kr) {
           open |= 1u << c;
           maxc = sh.ceil[c] > maxc ? sh.ceil[c] : maxc;
@@ -448,8 +624,8 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
         k = (int64_t)skey32[j];
         if (k < maxc) {
           vi = key_order[j];
-          h = Elem<DT>::f(col[vi]);
-          const int sa = res_slot<0>(h, e), sb = res_slot<1>(-h, e);
+          h = colv(vi);
+          const int sa = res_slot<0>(h, cp.e), sb = res_slot<1>(-h, cp.e);
           if (sa >= 0 && ((open >> sa) & 1u) && k < sh.ceil[sa]) sl[0] = sa;
           if (sb >= 0 && ((open >> sb) & 1u) && k < sh.ceil[sb]) sl[1] = sb;
         }
@@ -474,7 +650,7 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
         }
       }
       __syncthreads();
-      if (tid < 2 * kMaxB) {
+      if (tid < kSlots) {
         int t = 0;
 #pragma unroll
         for (int w = 0; w < kThreads / 32; ++w) {
@@ -493,53 +669,73 @@ __device__ __forceinline__ void dense_column(ColShared& sh, typename Elem<DT>::T
   flush_range(sh.st, kStage - n_res, n_res, res, err, &sh.base);
 }
 
-// Columns are taken grid-stride by at most one resident wave of CTAs, so an untriggered launch costs
-// about a wave of early exits rather than one CTA per column.
+// Hard columns are taken grid-stride from the strips' lists by at most one resident wave of CTAs,
+// so an untriggered launch, or one with no hard column, costs about a wave of early exits.
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 4)
-dense_column_kernel(const typename Elem<DT>::T* __restrict__ HT, int64_t ldh, int64_t n_v, const int64_t* __restrict__ tok,
-                    const uint32_t* __restrict__ key32, const uint32_t* __restrict__ skey32,
-                    const int32_t* __restrict__ key_order, int64_t layer, int64_t D,
-                    int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
-                    const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
-                    const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
-                    int64_t cap, int force, Lists top, Lists res, int32_t* __restrict__ err, int col_in_smem) {
+dense_hard_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
+                  int64_t n_v, const int64_t* __restrict__ tok, const int32_t* __restrict__ key_order, int64_t layer,
+                  int B, int64_t K, int64_t Kr, int reservoir, const float* __restrict__ top_seed,
+                  const int64_t* __restrict__ top_k, const int64_t* __restrict__ res_s,
+                  const int64_t* __restrict__ res_seed, const float* __restrict__ E, const int32_t* __restrict__ count,
+                  int64_t cap, int force, DenseWs ws, Lists top, Lists res, int32_t* __restrict__ err,
+                  int col_in_smem) {
   if (!triggered(count, cap, force)) return;
   extern __shared__ __align__(16) unsigned char col_raw[];
   ColShared& sh = *reinterpret_cast<ColShared*>(col_raw);
-  // with col_in_smem the column (ldh elements) is staged after the shared state
+  // with col_in_smem the column (n_v elements) is staged after the shared state
   auto* scol = col_in_smem ? reinterpret_cast<typename Elem<DT>::T*>(col_raw + ((sizeof(ColShared) + 15) / 16) * 16)
                            : nullptr;
-  for (int64_t d = blockIdx.x; d < D; d += gridDim.x) {
-    dense_column<DT>(sh, scol, d, HT, ldh, n_v, tok, key32, skey32, key_order, layer, D, B, K, Kr, reservoir, top_seed,
-                     top_k, res_s, res_seed, E, top, res, err);
+  const int S = (int)n_strips(D);
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int s = 0; s < S; ++s) {
+      sh.pre[s] = acc;
+      acc += ws.nhard[s];
+    }
+    sh.pre[S] = acc;
+  }
+  __syncthreads();
+  const int total = sh.pre[S];
+  for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    int s = 0;
+    while (sh.pre[s + 1] <= t) ++s;
+    const int64_t d = ws.hard[s * kStrip + (t - sh.pre[s])];
+    const uint32_t th = ws.tdec[d];
+    const uint32_t ordered = reservoir ? (ws.dec[d] >> 16) : 0u;
+    hard_column<DT>(sh, scol, d, H, ld, rows, n_v, tok, ws.skey32, key_order, layer, D, B, K, Kr, top_seed, top_k,
+                    res_s, res_seed, E, th, ordered, top, res, err);
     __syncthreads();  // the next column re-initialises the shared state and the staged column
   }
 }
 
 template <int DT>
-int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int32_t* valid_rows, int64_t n_v,
+int launch_dense(const void* Hv, int64_t D, int64_t ld, int64_t layer, const int32_t* valid_rows, int64_t n_v,
                  const int64_t* tok, const int64_t* key, const int32_t* key_order, int64_t B, int64_t K, int64_t Kr,
                  int reservoir, const float* top_seed, const int64_t* top_k, const int64_t* res_s,
                  const int64_t* res_seed, const float* E, const int32_t* count, int64_t cap, int force, Lists top,
                  Lists res, void* scratch, int32_t* err, cudaStream_t st) {
   using T = typename Elem<DT>::T;
-  const int64_t n8 = (n_v + 7) / 8 * 8;
-  T* HT = reinterpret_cast<T*>(scratch);
-  const int64_t ntiles = (n8 + 31) / 32 * ((D + 31) / 32);
-  const unsigned g1 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)num_sms() * 8));
-  // 32-bit keys in row order, then in key order, after the transposed copy (16-byte aligned:
-  // D * n8 * esize is a multiple of 16)
-  uint32_t* key32 = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(scratch) + D * n8 * (int64_t)sizeof(T));
-  uint32_t* skey32 = key32 + n8;
-  dense_gather_kernel<T><<<g1, dim3(32, 8), 0, st>>>(reinterpret_cast<const T*>(H), D, ld, valid_rows, n_v, n8, HT, n8,
-                                                     reservoir ? key : nullptr, key_order, reservoir ? key32 : nullptr,
-                                                     skey32, count, cap, force);
-  if (int e = check_launch("atlas_dense_select: gather")) return e;
-  // the column goes to shared memory when it fits next to the shared state (C4: ~62 KB of bf16 per
-  // column, two CTAs per SM); otherwise it is read from the transposed copy in global memory
+  const T* H = reinterpret_cast<const T*>(Hv);
+  const DenseWs ws = carve(scratch, n_v, D);
+  const int64_t S = n_strips(D);
+  // row ranges: about four resident 256-thread CTAs per SM over the strips, at least 64 rows and at
+  // most 65535 rows (16-bit per-thread counts) per range
+  int64_t R = std::max<int64_t>(1, ((int64_t)num_sms() * 4 + S - 1) / S);
+  R = std::min<int64_t>(R, std::max<int64_t>(1, n_v / 64));
+  R = std::max<int64_t>(R, (n_v + 65534) / 65535);
+  R = std::min<int64_t>(R, kRangesMax);
+  const dim3 g1((unsigned)S, (unsigned)R);
+  dense_count_kernel<DT><<<g1, kStrip, 0, st>>>(H, D, ld, valid_rows, n_v, tok, key, key_order, layer, (int)B, K, Kr,
+                                                reservoir, top_seed, top_k, res_s, res_seed, E, count, cap, force, ws);
+  if (int e = check_launch("atlas_dense_select: count")) return e;
+  dense_emit_kernel<DT><<<g1, kStrip, 0, st>>>(H, D, ld, valid_rows, n_v, tok, key, layer, (int)B, K, Kr, reservoir,
+                                               top_seed, top_k, res_s, res_seed, E, count, cap, force, ws, top, res, err);
+  if (int e = check_launch("atlas_dense_select: emit")) return e;
+  // the hard column goes to shared memory when it fits next to the shared state (C4: ~61 KB of bf16
+  // per column); otherwise every pass reads it from H
   const size_t base_smem = ((sizeof(ColShared) + 15) / 16) * 16;
-  const size_t col_bytes = (size_t)n8 * sizeof(T);
+  const size_t col_bytes = (size_t)((n_v + 7) / 8 * 8) * sizeof(T);
   const int col_in_smem = base_smem + col_bytes <= (size_t)kDenseSmemMax ? 1 : 0;
   const size_t smem = col_in_smem ? base_smem + col_bytes : sizeof(ColShared);
   // the attribute is set once per device and instantiation (this launch runs once per layer and
@@ -548,7 +744,7 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    if (cudaFuncSetAttribute(dense_column_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDenseSmemMax) !=
+    if (cudaFuncSetAttribute(dense_hard_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDenseSmemMax) !=
         cudaSuccess)
       return fail(ATLAS_ERR_CUDA, "dense_select: cannot reserve %zu bytes of shared memory", smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
@@ -557,11 +753,11 @@ int launch_dense(const void* H, int64_t D, int64_t ld, int64_t layer, const int3
   // fit in the SM's 228 KB (1 KB of it reserved per CTA)
   int per_sm = (int)(((size_t)228 * 1024) / (smem + 1024));
   per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
-  const unsigned g2 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
-  dense_column_kernel<DT><<<g2, kThreads, smem, st>>>(HT, n8, n_v, tok, key32, skey32, key_order, layer, D, (int)B, K, Kr,
-                                                                reservoir, top_seed, top_k, res_s, res_seed, E, count,
-                                                                cap, force, top, res, err, col_in_smem);
-  return check_launch("atlas_dense_select: column");
+  const unsigned g3 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
+  dense_hard_kernel<DT><<<g3, kThreads, smem, st>>>(H, D, ld, valid_rows, n_v, tok, key_order, layer, (int)B, K, Kr,
+                                                    reservoir, top_seed, top_k, res_s, res_seed, E, count, cap, force,
+                                                    ws, top, res, err, col_in_smem);
+  return check_launch("atlas_dense_select: hard columns");
 }
 
 int esize(int dtype) { return dtype == ATLAS_F32 ? 4 : 2; }
@@ -573,8 +769,8 @@ using namespace atlas;
 
 extern "C" int64_t atlas_dense_scratch_bytes(int64_t n_v, int64_t D, int64_t B, int dtype) {
   (void)B;
-  const int64_t n8 = (n_v + 7) / 8 * 8;
-  return D * n8 * esize(dtype) + n8 * 8 + 256;  // transposed valid rows, 32-bit keys in row and key order
+  (void)dtype;
+  return ws_bytes(n_v, D);  // partial counts, decisions, hard-column lists, keys in key order
 }
 
 extern "C" int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D, int64_t ld, int64_t layer,
@@ -591,7 +787,10 @@ extern "C" int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D
                 kMaxB);
   ATLAS_REQUIRE(2 * K + 2 * B * Kr <= kStage, "dense_select: K/Kr too large for the staging area");
   ATLAS_REQUIRE((layer * 2 + 2) * D * B < (1LL << 31) && n_v < (1LL << 31), "dense_select: ids exceed int32");
-  ATLAS_REQUIRE(n_v <= (int64_t)kThreads * 65535, "dense_select: more than %d valid rows", kThreads * 65535);
+  ATLAS_REQUIRE(n_v <= (int64_t)kRangesMax * 65535, "dense_select: more than %lld valid rows",
+                (long long)kRangesMax * 65535);
+  ATLAS_REQUIRE(n_strips(D) <= kRangesMax * 4, "dense_select: D above %d", kRangesMax * 4 * kStrip);
+  (void)esize;
   (void)flag;
   if (n_v == 0) return ATLAS_OK;
   ATLAS_REQUIRE(force || count, "dense_select: count required unless forced");

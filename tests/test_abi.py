@@ -36,7 +36,9 @@ def test_workspace_size_queries():
     lib = _lib.load()
     assert lib.atlas_merge_ws_i32(4096, 100) >= 4 * 4096
     assert lib.atlas_merge_ws_bytes(1000) >= 20 * 1000
-    assert lib.atlas_dense_scratch_bytes(32768, 5120, 5, 1) >= 32768 * 5120 * 2
+    # per-range partial counts (64 ranges x 18 counts x D), decisions, hard-column lists, keys in key order
+    assert lib.atlas_dense_scratch_bytes(32768, 5120, 5, 1) >= 64 * 18 * 5120 * 4 + 32768 * 4
+    assert lib.atlas_dense_scratch_bytes(65536, 5120, 5, 1) > lib.atlas_dense_scratch_bytes(32768, 5120, 5, 1)
 
 
 def test_product_refuses_cpu_device():
