@@ -380,48 +380,68 @@ def kernel_microbench(dev, peaks, reps=20):
 def dense_burst(dev, peaks, scale, shift, T=32768, D=5120, batches=6):
     """The dense burst path at C4 shapes: one layer of [32768 x 5120] bf16 activations (Student-t(3)
     x scale + shift, fresh values every batch, 8% padding rows), K=100, Kr=32, 5 bins, forced dense in
-    every batch (naive mode), as a layer whose compaction buffer overflowed takes it. Times
-    atlas_dense_select (row-major count and emit passes over H, then the per-column exact top-K
-    select and key-order walks of the columns that need them) with CUDA events: the first batch
-    meets an empty state (every column runs its radix select), the later ones a full state (few
-    admissible candidates per column). GB/s are activation bytes consumed
-    per second, and the fraction of HBM counts the two row-major passes over n_v x D x 2 bytes."""
+    every batch, as a layer whose compaction buffer overflowed takes it. Times atlas_dense_select
+    (row-major count and emit passes over H, then the per-column exact top-K select and key-order
+    walks of the columns that need them) with CUDA events, in two states:
+      * unseeded: the first batch meets an empty state (every column runs its radix select and every
+        bin walks the key order), the later ones a state that fills batch by batch;
+      * seeded as the C4 stream is (top-K seed at the 1 - 2K/660k quantile of a pilot, i.e. the
+        2000-sequence pilot's 2K-th largest value; reservoir key ceilings sized for the 190M-token
+        stream), which is the state a burst meets in the C4 run.
+    GB/s are activation bytes consumed per second; the fraction of HBM counts the two row-major
+    passes over n_v x D x 2 bytes."""
     from proteus_b200.core import Atlas, AtlasConfig
+    from proteus_b200.pilot import pilot_seeds
     qs = torch.tensor([0.5, 0.9, 0.99, 0.999, 0.9999], device=dev)
     t3 = torch.distributions.StudentT(torch.tensor(3.0, device=dev))
     H = (t3.sample((T, D)) * scale + shift).to(torch.bfloat16)
-    E = torch.stack([torch.quantile(H[:4096].float(), qs, dim=0).T, torch.quantile(-H[:4096].float(), qs, dim=0).T])
-    at = Atlas(1, D, E.unsqueeze(0).contiguous(), AtlasConfig(K=100, Kr=32, seed=0, subsample=False, gram=False,
-                                                             naive=True), device=dev)
+    pilot_H = H[:16384].float()
+    E = torch.stack([torch.quantile(pilot_H[:4096], qs, dim=0).T, torch.quantile(-pilot_H[:4096], qs, dim=0).T])
+    q = 1.0 - 200 / 660_000
+    top = torch.stack([torch.quantile(pilot_H, q, dim=0), torch.quantile(-pilot_H, q, dim=0)])
+    ts = torch.nextafter(top, torch.full_like(top, float("-inf"))).view(1, 2, D)
+    _, rk = pilot_seeds([pilot_H], E.unsqueeze(0).contiguous(), 100, 32, 190_000_000)
+    del pilot_H
     Lmax = 256
     valid = torch.cat([r * Lmax + 1 + torch.arange(Lmax - 2 - (r % 37)) for r in range(T // Lmax)])
     n_v = valid.numel()
-    times = []
-    for i in range(batches):
-        if i:
-            H.copy_((t3.sample((T, D)) * scale + shift).to(torch.bfloat16))
-        seq = torch.div(valid, Lmax, rounding_mode="floor") + (T // Lmax) * i
-        tok = seq * 1024 + (valid % Lmax) - 1
-        ctx = at.make_ctx(T, valid, tok)
-        kt = KernelTimer()
-        at.kernel_timer = kt
-        at.begin_batch(ctx)
-        at.observe(0, H)
-        at.end_batch()
-        at.kernel_timer = None
-        torch.cuda.synchronize()
-        times.append(kt.total_ms("dense"))
-    at.check_errors()
     h_bytes = n_v * D * 2
-    later = sorted(times[2:]) if len(times) > 2 else times[1:]
-    ms_later = later[len(later) // 2]
+
+    def run(seeded):
+        at = Atlas(1, D, E.unsqueeze(0).contiguous(), AtlasConfig(K=100, Kr=32, seed=0, subsample=False, gram=False,
+                                                                 naive=True), device=dev)
+        if seeded:
+            at.seed(ts, rk)
+            at._dense_layers = {0}  # seeding clears the dense-first layers; this burst forces the layer dense
+        times = []
+        for i in range(batches):
+            H.copy_((t3.sample((T, D)) * scale + shift).to(torch.bfloat16))
+            seq = torch.div(valid, Lmax, rounding_mode="floor") + (T // Lmax) * i
+            tok = seq * 1024 + (valid % Lmax) - 1
+            ctx = at.make_ctx(T, valid, tok)
+            kt = KernelTimer()
+            at.kernel_timer = kt
+            at.begin_batch(ctx)
+            at.observe(0, H)
+            at.end_batch()
+            at.kernel_timer = None
+            torch.cuda.synchronize()
+            times.append(kt.total_ms("dense"))
+        at.check_errors()
+        later = sorted(times[2:]) if len(times) > 2 else times[1:]
+        ms_later = later[len(later) // 2]
+        out = {"ms_first_batch": times[0], "ms_later_batches_median": ms_later,
+               "H_GBps_later": h_bytes / ms_later / 1e6,
+               "frac_hbm_2_passes_first": 2 * h_bytes / times[0] / 1e6 / peaks["hbm_gbs"],
+               "frac_hbm_2_passes_later": 2 * h_bytes / ms_later / 1e6 / peaks["hbm_gbs"],
+               "ms_per_batch": times, "dense_layer_batches": at.stats["dense_layer_batches"],
+               "top_cand_per_batch": at.stats["top_cand"] / batches, "res_cand_per_batch": at.stats["res_cand"] / batches}
+        del at
+        return out
+
     res = {"valid_rows": n_v, "D": D, "K": 100, "Kr": 32, "batches": batches,
-           "ms_first_batch_empty_state": times[0], "ms_later_batches_median": ms_later,
-           "H_GBps_first": h_bytes / times[0] / 1e6, "H_GBps_later": h_bytes / ms_later / 1e6,
-           "frac_hbm_2_passes_first": 2 * h_bytes / times[0] / 1e6 / peaks["hbm_gbs"],
-           "frac_hbm_2_passes_later": 2 * h_bytes / ms_later / 1e6 / peaks["hbm_gbs"],
-           "ms_per_batch": times, "dense_layer_batches": at.stats["dense_layer_batches"]}
-    del H, at
+           "unseeded": run(False), "seeded_c4": run(True)}
+    del H
     torch.cuda.empty_cache()
     return res
 

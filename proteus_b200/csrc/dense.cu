@@ -140,25 +140,30 @@ __device__ __forceinline__ int64_t slot_ceiling(int slot, bool ok, int64_t layer
   return (th == kI64Min) ? (1ll << 32) : -th;
 }
 
-// Admissible top-K candidate: s > seed and top_key(s, tok) above the state's K-th key (token ids are
-// read only on a tie of the value part).
-__device__ __forceinline__ bool top_candidate(float s, float seed, uint64_t ku, const int64_t* __restrict__ tok,
-                                              int64_t i) {
-  if (!(s > seed)) return false;
+// Admissible top-K candidate once s > seed holds: top_key(s, tok) above the state's K-th key (token
+// ids are read only on a tie of the value part).
+__device__ __forceinline__ bool top_above(float s, uint64_t ku, const int64_t* __restrict__ tok, int64_t i) {
   const uint32_t hi = key_hi(s), khi = (uint32_t)(ku >> 32);
   if (hi != khi) return hi > khi;
   const uint64_t c = ((uint64_t)hi << 32) | (uint64_t)(kM32 - (uint32_t)tok[i]);
   return c > ku;
 }
 
-// Reservoir slot (p * kMaxB + bin) of value s for pole P, or -1 below the pole's lowest edge.
-template <int P>
-__device__ __forceinline__ int res_slot(float s, const float (&e)[2][kMaxB]) {
-  if (!(s >= e[P][0])) return -1;
+// Bin of s (at or above the lowest edge) among NB edges; unused edges (NB = kMaxB with B < kMaxB) are
+// NaN and never counted.
+template <int NB>
+__device__ __forceinline__ int bin_in(float s, const float (&ep)[kMaxB]) {
   int bin = 0;
 #pragma unroll
-  for (int b = 1; b < kMaxB; ++b) bin += (s >= e[P][b]) ? 1 : 0;
-  return P * kMaxB + bin;
+  for (int b = 1; b < NB; ++b) bin += (s >= ep[b]) ? 1 : 0;
+  return bin;
+}
+
+// Reservoir slot (p * kMaxB + bin) of value s for pole P, or -1 below the pole's lowest edge.
+template <int P, int NB>
+__device__ __forceinline__ int res_slot(float s, const float (&e)[2][kMaxB]) {
+  if (!(s >= e[P][0])) return -1;
+  return P * kMaxB + bin_in<NB>(s, e[P]);
 }
 
 // Row range r of R over n_v rows.
@@ -168,7 +173,7 @@ __device__ __forceinline__ void row_range(int64_t n_v, int r, int R, int64_t& i0
 }
 
 // ------------------------------------------------------------------------------------ 1. count
-template <int DT>
+template <int DT, int NB>
 __global__ void __launch_bounds__(kStrip, 4)
 dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
                    int64_t n_v, const int64_t* __restrict__ tok, const int64_t* __restrict__ key,
@@ -192,8 +197,13 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
   }
   ColParams cp;
   load_params(cp, ok, layer, D, d, B, K, reservoir, top_seed, top_k, E);
+  int64_t maxc = 0;  // rows whose key is at or above every ceiling of the column skip the bins
 #pragma unroll
-  for (int s = 0; s < kSlots; ++s) s_ceil[s][tid] = slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed);
+  for (int s = 0; s < kSlots; ++s) {
+    const int64_t c = slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed);
+    s_ceil[s][tid] = c;
+    maxc = c > maxc ? c : maxc;
+  }
   int64_t i0, i1;
   row_range(n_v, r, R, i0, i1);
   int c0 = 0, c1 = 0;
@@ -212,17 +222,22 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
     for (int u = 0; u < kU; ++u) {
       if (i + u >= i1) break;
       const float h = Elem<DT>::f(x[u]);
-      c0 += top_candidate(h, cp.seed[0], cp.ku[0], tok, i + u) ? 1 : 0;
-      c1 += top_candidate(-h, cp.seed[1], cp.ku[1], tok, i + u) ? 1 : 0;
-      if (reservoir) {
-        const int sa = res_slot<0>(h, cp.e), sb = res_slot<1>(-h, cp.e);
-        if (sa >= 0 && kk[u] < s_ceil[sa][tid]) {
-          const uint64_t inc = 1ull << (16 * (sa & 3));
-          if (sa < 4) rc[0][0] += inc; else rc[0][1] += inc;
+      if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, i + u)) ++c0;
+      if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, i + u)) ++c1;
+      if (kk[u] < maxc) {  // maxc is 0 without a reservoir
+        if (h >= cp.e[0][0]) {
+          const int b = bin_in<NB>(h, cp.e[0]);
+          if (kk[u] < s_ceil[b][tid]) {
+            const uint64_t inc = 1ull << (16 * (b & 3));
+            if (b < 4) rc[0][0] += inc; else rc[0][1] += inc;
+          }
         }
-        if (sb >= 0 && kk[u] < s_ceil[sb][tid]) {
-          const uint64_t inc = 1ull << (16 * (sb & 3));
-          if (sb < kMaxB + 4) rc[1][0] += inc; else rc[1][1] += inc;
+        if (-h >= cp.e[1][0]) {
+          const int b = bin_in<NB>(-h, cp.e[1]);
+          if (kk[u] < s_ceil[kMaxB + b][tid]) {
+            const uint64_t inc = 1ull << (16 * (b & 3));
+            if (b < 4) rc[1][0] += inc; else rc[1][1] += inc;
+          }
         }
       }
     }
@@ -307,7 +322,7 @@ __device__ __forceinline__ void emit_rec(EmitStage& es, int w, const Lists& o, i
   }
 }
 
-template <int DT>
+template <int DT, int NB>
 __global__ void __launch_bounds__(kStrip, 4)
 dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
                   int64_t n_v, const int64_t* __restrict__ tok, const int64_t* __restrict__ key, int64_t layer, int B,
@@ -329,9 +344,13 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
   load_params(cp, ok, layer, D, d, B, K, reservoir, top_seed, top_k, E);
   if (th & 1u) cp.seed[0] = __int_as_float(0x7F800000);  // pole emitted by the hard-column kernel
   if (th & 2u) cp.seed[1] = __int_as_float(0x7F800000);
+  int64_t maxc = 0;  // the largest ceiling of the direct slots (0: no reservoir record here)
 #pragma unroll
-  for (int s = 0; s < kSlots; ++s)
-    s_ceil[s][tid] = ((direct >> s) & 1u) ? slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed) : 0;
+  for (int s = 0; s < kSlots; ++s) {
+    const int64_t c = ((direct >> s) & 1u) ? slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed) : 0;
+    s_ceil[s][tid] = c;
+    maxc = c > maxc ? c : maxc;
+  }
   if (tid < 2) es.n[tid] = 0;
   __syncthreads();
   const bool any = __syncthreads_or(ok && (((th & 3u) != 3u) || direct != 0)) != 0;
@@ -342,35 +361,39 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
     const int32_t g0 = (int32_t)((layer * 2) * D + d), g1 = (int32_t)((layer * 2 + 1) * D + d);
     for (int64_t i = i0; i < i1; i += kU) {
       T x[kU];
+      int64_t kk[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const int64_t ii = i + u < i1 ? i + u : i1 - 1;
         x[u] = Hc[(int64_t)rows[ii] * ld];
+        kk[u] = reservoir ? key[ii] : 0;
       }
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         if (i + u >= i1) break;
         const int64_t ii = i + u;
         const float h = Elem<DT>::f(x[u]);
-        if (top_candidate(h, cp.seed[0], cp.ku[0], tok, ii)) {
+        if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, ii)) {
           const int64_t t = tok[ii];
           const int64_t k64 = (int64_t)((((uint64_t)key_hi(h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
                                         0x8000000000000000ull);
           emit_rec(es, 0, top, g0, k64, t, h, err);
         }
-        if (top_candidate(-h, cp.seed[1], cp.ku[1], tok, ii)) {
+        if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, ii)) {
           const int64_t t = tok[ii];
           const int64_t k64 = (int64_t)((((uint64_t)key_hi(-h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
                                         0x8000000000000000ull);
           emit_rec(es, 0, top, g1, k64, t, -h, err);
         }
-        if (direct) {
-          const int sa = res_slot<0>(h, cp.e), sb = res_slot<1>(-h, cp.e);
-          const bool da = sa >= 0 && ((direct >> sa) & 1u), db = sb >= 0 && ((direct >> sb) & 1u);
-          if (da || db) {
-            const int64_t k = (int64_t)(uint32_t)key[ii];
-            if (da && k < s_ceil[sa][tid]) emit_rec(es, 1, res, g0 * B + sa, -k, tok[ii], h, err);
-            if (db && k < s_ceil[sb][tid]) emit_rec(es, 1, res, g1 * B + (sb - kMaxB), -k, tok[ii], h, err);
+        const int64_t k = kk[u];
+        if (k < maxc) {  // non-direct slots have ceiling 0 here, so they never admit
+          if (h >= cp.e[0][0]) {
+            const int b = bin_in<NB>(h, cp.e[0]);
+            if (k < s_ceil[b][tid]) emit_rec(es, 1, res, g0 * B + b, -k, tok[ii], h, err);
+          }
+          if (-h >= cp.e[1][0]) {
+            const int b = bin_in<NB>(-h, cp.e[1]);
+            if (k < s_ceil[kMaxB + b][tid]) emit_rec(es, 1, res, g1 * B + b, -k, tok[ii], h, err);
           }
         }
       }
@@ -459,7 +482,7 @@ struct ColShared {
 
 // One hard column d (the CTA's threads together): the poles flagged in th take the radix select and
 // emit their top-K records; the slots flagged in `ordered` take their first Kr rows in key order.
-template <int DT>
+template <int DT, int NB>
 __device__ __forceinline__ void hard_column(ColShared& sh, typename Elem<DT>::T* scol, int64_t d,
                                             const typename Elem<DT>::T* __restrict__ H, int64_t ld,
                                             const int32_t* __restrict__ rows, int64_t n_v,
@@ -625,7 +648,7 @@ __device__ __forceinline__ void hard_column(ColShared& sh, typename Elem<DT>::T*
         if (k < maxc) {
           vi = key_order[j];
           h = colv(vi);
-          const int sa = res_slot<0>(h, cp.e), sb = res_slot<1>(-h, cp.e);
+          const int sa = res_slot<0, NB>(h, cp.e), sb = res_slot<1, NB>(-h, cp.e);
           if (sa >= 0 && ((open >> sa) & 1u) && k < sh.ceil[sa]) sl[0] = sa;
           if (sb >= 0 && ((open >> sb) & 1u) && k < sh.ceil[sb]) sl[1] = sb;
         }
@@ -671,7 +694,7 @@ __device__ __forceinline__ void hard_column(ColShared& sh, typename Elem<DT>::T*
 
 // Hard columns are taken grid-stride from the strips' lists by at most one resident wave of CTAs,
 // so an untriggered launch, or one with no hard column, costs about a wave of early exits.
-template <int DT>
+template <int DT, int NB>
 __global__ void __launch_bounds__(kThreads, 4)
 dense_hard_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
                   int64_t n_v, const int64_t* __restrict__ tok, const int32_t* __restrict__ key_order, int64_t layer,
@@ -703,13 +726,13 @@ dense_hard_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
     const int64_t d = ws.hard[s * kStrip + (t - sh.pre[s])];
     const uint32_t th = ws.tdec[d];
     const uint32_t ordered = reservoir ? (ws.dec[d] >> 16) : 0u;
-    hard_column<DT>(sh, scol, d, H, ld, rows, n_v, tok, ws.skey32, key_order, layer, D, B, K, Kr, top_seed, top_k,
+    hard_column<DT, NB>(sh, scol, d, H, ld, rows, n_v, tok, ws.skey32, key_order, layer, D, B, K, Kr, top_seed, top_k,
                     res_s, res_seed, E, th, ordered, top, res, err);
     __syncthreads();  // the next column re-initialises the shared state and the staged column
   }
 }
 
-template <int DT>
+template <int DT, int NB>
 int launch_dense(const void* Hv, int64_t D, int64_t ld, int64_t layer, const int32_t* valid_rows, int64_t n_v,
                  const int64_t* tok, const int64_t* key, const int32_t* key_order, int64_t B, int64_t K, int64_t Kr,
                  int reservoir, const float* top_seed, const int64_t* top_k, const int64_t* res_s,
@@ -726,10 +749,10 @@ int launch_dense(const void* Hv, int64_t D, int64_t ld, int64_t layer, const int
   R = std::max<int64_t>(R, (n_v + 65534) / 65535);
   R = std::min<int64_t>(R, kRangesMax);
   const dim3 g1((unsigned)S, (unsigned)R);
-  dense_count_kernel<DT><<<g1, kStrip, 0, st>>>(H, D, ld, valid_rows, n_v, tok, key, key_order, layer, (int)B, K, Kr,
+  dense_count_kernel<DT, NB><<<g1, kStrip, 0, st>>>(H, D, ld, valid_rows, n_v, tok, key, key_order, layer, (int)B, K, Kr,
                                                 reservoir, top_seed, top_k, res_s, res_seed, E, count, cap, force, ws);
   if (int e = check_launch("atlas_dense_select: count")) return e;
-  dense_emit_kernel<DT><<<g1, kStrip, 0, st>>>(H, D, ld, valid_rows, n_v, tok, key, layer, (int)B, K, Kr, reservoir,
+  dense_emit_kernel<DT, NB><<<g1, kStrip, 0, st>>>(H, D, ld, valid_rows, n_v, tok, key, layer, (int)B, K, Kr, reservoir,
                                                top_seed, top_k, res_s, res_seed, E, count, cap, force, ws, top, res, err);
   if (int e = check_launch("atlas_dense_select: emit")) return e;
   // the hard column goes to shared memory when it fits next to the shared state (C4: ~61 KB of bf16
@@ -744,7 +767,7 @@ int launch_dense(const void* Hv, int64_t D, int64_t ld, int64_t layer, const int
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    if (cudaFuncSetAttribute(dense_hard_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDenseSmemMax) !=
+    if (cudaFuncSetAttribute(dense_hard_kernel<DT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDenseSmemMax) !=
         cudaSuccess)
       return fail(ATLAS_ERR_CUDA, "dense_select: cannot reserve %zu bytes of shared memory", smem);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
@@ -754,7 +777,7 @@ int launch_dense(const void* Hv, int64_t D, int64_t ld, int64_t layer, const int
   int per_sm = (int)(((size_t)228 * 1024) / (smem + 1024));
   per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
   const unsigned g3 = (unsigned)std::max<int64_t>(1, std::min<int64_t>(D, (int64_t)num_sms() * per_sm));
-  dense_hard_kernel<DT><<<g3, kThreads, smem, st>>>(H, D, ld, valid_rows, n_v, tok, key_order, layer, (int)B, K, Kr,
+  dense_hard_kernel<DT, NB><<<g3, kThreads, smem, st>>>(H, D, ld, valid_rows, n_v, tok, key_order, layer, (int)B, K, Kr,
                                                     reservoir, top_seed, top_k, res_s, res_seed, E, count, cap, force,
                                                     ws, top, res, err, col_in_smem);
   return check_launch("atlas_dense_select: hard columns");
@@ -805,17 +828,19 @@ extern "C" int atlas_dense_select(const void* H, int dtype, int64_t T, int64_t D
   Lists res{res_g, res_sc, res_tok, res_val, n_res, res_cap};
   const int32_t* cnt = count ? count : n_top;  // never read when forced
   cudaStream_t st = (cudaStream_t)stream;
+  // bins: B = 5 (the reference's default edges) compiled exactly, other B on kMaxB NaN-padded edges
+#define ATLAS_DENSE_CALL(DT, NB)                                                                                   \
+  launch_dense<DT, NB>(H, D, ld, layer, valid_rows, n_v, tok, key, key_order, B, K, Kr, reservoir, top_seed, top_k, \
+                       res_s, res_seed, E, cnt, cap, force, top, res, scratch, err, st)
   switch (dtype) {
     case ATLAS_BF16:
-      return launch_dense<ATLAS_BF16>(H, D, ld, layer, valid_rows, n_v, tok, key, key_order, B, K, Kr, reservoir, top_seed,
-                                      top_k, res_s, res_seed, E, cnt, cap, force, top, res, scratch, err, st);
+      return B == 5 ? ATLAS_DENSE_CALL(ATLAS_BF16, 5) : ATLAS_DENSE_CALL(ATLAS_BF16, kMaxB);
     case ATLAS_F16:
-      return launch_dense<ATLAS_F16>(H, D, ld, layer, valid_rows, n_v, tok, key, key_order, B, K, Kr, reservoir, top_seed,
-                                     top_k, res_s, res_seed, E, cnt, cap, force, top, res, scratch, err, st);
+      return B == 5 ? ATLAS_DENSE_CALL(ATLAS_F16, 5) : ATLAS_DENSE_CALL(ATLAS_F16, kMaxB);
     case ATLAS_F32:
-      return launch_dense<ATLAS_F32>(H, D, ld, layer, valid_rows, n_v, tok, key, key_order, B, K, Kr, reservoir, top_seed,
-                                     top_k, res_s, res_seed, E, cnt, cap, force, top, res, scratch, err, st);
+      return B == 5 ? ATLAS_DENSE_CALL(ATLAS_F32, 5) : ATLAS_DENSE_CALL(ATLAS_F32, kMaxB);
     default:
       return fail(ATLAS_ERR_ARG, "dense_select: unknown dtype %d", dtype);
   }
+#undef ATLAS_DENSE_CALL
 }
