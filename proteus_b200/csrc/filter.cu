@@ -310,12 +310,18 @@ constexpr int kBWarps = 8;                       // consumer warps (4 rows of a 
 constexpr int kBThreads = (kBWarps + 1) * 32;
 constexpr int kBCtasPerSm = ATLAS_FILTER_BCTAS;
 constexpr int kBSeg = 512;                       // bytes of one row segment (256 bf16 columns)
-constexpr int kBStage = 1024;                    // staged survivors per CTA (12 KB)
+#ifndef ATLAS_FILTER_BSTAGE_N
+#define ATLAS_FILTER_BSTAGE_N 1024
+#endif
+constexpr int kBStage = ATLAS_FILTER_BSTAGE_N;   // staged survivors per CTA (12 bytes each)
 
 #ifndef ATLAS_FILTER_QUEUE
 #define ATLAS_FILTER_QUEUE 1
 #endif
-constexpr int kBQueue = 64;  // flagged row vectors parked per consumer warp
+#ifndef ATLAS_FILTER_BQUEUE
+#define ATLAS_FILTER_BQUEUE 64
+#endif
+constexpr int kBQueue = ATLAS_FILTER_BQUEUE;  // flagged row vectors parked per consumer warp
 
 // Flagged row vectors of one consumer warp, waiting for extraction: the 16 bytes, the row-map entry
 // and the lane (the lane gives the 8 columns and their thresholds).

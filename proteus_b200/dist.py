@@ -41,7 +41,7 @@ class Lockstep:
     knows whether any rank still has work. Ranks whose shard is exhausted keep calling `agree`
     (without a batch) until every shard is, so all ranks leave the loop at the same step and enter
     the combine together, and a stop taken by one rank is taken by all. One all-reduce of two ints
-    per batch (a host read: the one synchronisation per batch that the loop already makes)."""
+    per batch; given a host (gloo) group and no device, it never waits for a GPU stream."""
 
     def __init__(self, group=None, device=None):
         self.group = group

@@ -4,8 +4,9 @@
   torchrun --nproc-per-node 8 -m proteus_b200.run_atlas ...   (one shard of the batch plan per GPU)
 
 Outputs in --out (as the reference, run_atlas.py:3-8): ckpt/ckpt_<batch>.pt (atomic, last 2 kept),
-batches.jsonl (one record per batch), run.json (summary), atlas.pt (final result + sha256 digests of
-the exact fields). With several ranks each rank checkpoints its own shard under ckpt/rank<r>/ and
+batches.jsonl (one record per batch; its GPU times come from CUDA events read a few batches later,
+so the loop never drains the GPU to time a batch), run.json (summary), atlas.pt (final result +
+sha256 digests of the exact fields). With several ranks each rank checkpoints its own shard under ckpt/rank<r>/ and
 the shard states are combined exactly (proteus_b200.dist.merge_states) before rank 0 writes atlas.pt.
 
 --data accepts the reference's Swiss-Prot .pt format or `synthetic:<n_seq>[:<seed>]` (C4-like
@@ -287,9 +288,12 @@ def main(argv=None):
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800),
                                              device_id=torch.device("cuda", local))
+        # the per-batch stop agreement runs on the host (gloo), so it never waits for the GPU stream
+        ctl_group = torch.distributed.new_group(backend="gloo", timeout=datetime.timedelta(seconds=1800))
         dev = f"cuda:{local}"
     else:
         dev = a.device
+        ctl_group = None
     out = Path(a.out)
     ck_dir = out / "ckpt" if world == 1 else out / "ckpt" / f"rank{rank}"
     ck_dir.mkdir(parents=True, exist_ok=True)
@@ -395,12 +399,46 @@ def main(argv=None):
     # cap stops all ranks at the same step, and ranks whose shard is exhausted wait for the others,
     # so no rank enters the combine's collectives while another still streams or has returned
     from .dist import Lockstep
-    lock = Lockstep(device=dev if world > 1 else None)
+    lock = Lockstep(group=ctl_group)
     STOP_CAP, STOP_DEADLINE = 1, 2
 
     def finish_process_group():
         if world > 1:
             torch.distributed.destroy_process_group()
+
+    # Per-batch records are timed by CUDA events on the loop's stream and written once the events
+    # have completed (a lag of up to `lag` batches), so the loop never drains the GPU to time a
+    # batch; the host stays ahead and the GPU stays busy. The paired hook-free forward is timed the
+    # same way.
+    pending = []  # [rec, start event, atlas-pass start, atlas-pass end, paired-forward events or None]
+    lag = 2
+
+    def ev():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def drain(keep: int):
+        """Write the records of completed batches; wait for all but the last `keep`."""
+        nonlocal batch_s
+        while pending:
+            rec, e0, ea, eb, fe = pending[0]
+            if len(pending) > keep:
+                eb.synchronize()
+            elif not eb.query():
+                break
+            pending.pop(0)
+            atlas_s = ea.elapsed_time(eb) / 1e3
+            fwd_s = fe[0].elapsed_time(fe[1]) / 1e3 if fe is not None else None
+            rec.update({"seconds": e0.elapsed_time(eb) / 1e3, "fwd_only_s": fwd_s, "atlas_pass_s": atlas_s,
+                        "overhead_vs_fwd": (atlas_s / fwd_s - 1) if fwd_s else None})
+            if fwd_s:
+                paired.append((rec["batch"] * world + rank, atlas_s / fwd_s - 1))
+            if rec["n_done"] > 2:
+                batch_s = max(batch_s, rec["seconds"])
+            del rec["n_done"]
+            logf.write(json.dumps(rec) + "\n")
+        logf.flush()
 
     def _stream(src_iter):
         """The batch loop; returns the agreed stop code (None after the whole plan)."""
@@ -412,15 +450,14 @@ def main(argv=None):
             if item is not None:
                 b, ctx_host = item
                 tb = time.time()
+                e0 = ev()
                 ids, am = b.input_ids.to(dev, non_blocking=True), b.attention_mask.to(dev, non_blocking=True)
-                fwd_s = None
+                fe = None
                 if a.pair_forward or (a.pair_every and bi % a.pair_every == 0):
                     atlas.enabled = False
-                    sync(dev)
-                    tf0 = time.time()
+                    f0 = ev()
                     model(input_ids=ids, attention_mask=am)
-                    sync(dev)
-                    fwd_s = time.time() - tf0
+                    fe = (f0, ev())
                     atlas.enabled = True
                 prof = None
                 if bi in a.profile_at:
@@ -429,7 +466,9 @@ def main(argv=None):
                         acts.append(torch.profiler.ProfilerActivity.CUDA)
                     prof = torch.profiler.profile(activities=acts)
                     prof.__enter__()
-                ta0 = time.time()
+                if prof is not None:
+                    sync(dev)
+                ea = ev()
                 if ctx_host is not None:
                     ctx = ctx_host.to(dev)
                 elif a.host_ctx:
@@ -444,28 +483,27 @@ def main(argv=None):
                 gram_flushed = bi % a.gram_flush_every == a.gram_flush_every - 1
                 if gram_flushed:
                     atlas.flush_gram()
-                sync(dev)
-                atlas_s = time.time() - ta0
+                eb = ev()
                 if prof is not None:
+                    sync(dev)
                     prof.__exit__(None, None, None)
                     write_profile(prof, out / f"profile_batch_{bi}.txt", dev)
                     log(f"[atlas] profiled batch {bi} -> profile_batch_{bi}.txt")
+                # seconds (start of the batch to the end of its atlas pass), fwd_only_s, atlas_pass_s
+                # and overhead_vs_fwd are filled from the events by drain()
                 rec = {"batch": bi, "n_seen_before": n_before, "n_valid": ctx.n_v, "rows": b.n_rows,
-                       "Lmax": int(b.input_ids.shape[1]), "seconds": time.time() - tb, "t_start": tb,
-                       "t_end": time.time(), "fwd_only_s": fwd_s, "atlas_pass_s": atlas_s,
-                       "overhead_vs_fwd": (atlas_s / fwd_s - 1) if fwd_s else None, "gram_flushed": gram_flushed,
-                       "flops": flops_per_batch(info, b.n_rows, b.input_ids.shape[1]), "redo_layers": []}
-                if fwd_s:
-                    paired.append((bi * world + rank, atlas_s / fwd_s - 1))
+                       "Lmax": int(b.input_ids.shape[1]), "t_enqueue_start": tb, "t_enqueue_end": time.time(),
+                       "gram_flushed": gram_flushed, "flops": flops_per_batch(info, b.n_rows, b.input_ids.shape[1]),
+                       "redo_layers": [], "n_done": n_done}
                 n_done += 1
                 bi += 1
                 last_ckpt_s = None
                 if bi % a.ckpt_every == 0:
+                    drain(0)
                     save_ckpt(bi)
                 rec["ckpt_s"] = last_ckpt_s
-                logf.write(json.dumps(rec) + "\n")
-                logf.flush()
-                batch_s = max(batch_s, rec["seconds"]) if n_done > 2 else batch_s
+                pending.append([rec, e0, ea, eb, fe])
+                drain(lag)
                 item = next(src_iter, None)
                 if a.deadline and item is not None and \
                         time.time() > a.deadline - 2 * (batch_s + max(ckpt_s, 30.0)):
@@ -473,6 +511,8 @@ def main(argv=None):
                 elif a.stop_after and n_done >= a.stop_after:
                     want = STOP_CAP
             code, more = lock.agree(want, item is not None)
+            if code or not more:
+                drain(0)
             if code == STOP_DEADLINE:
                 if bi % a.ckpt_every:
                     save_ckpt(bi)
@@ -494,6 +534,8 @@ def main(argv=None):
     def with_ctx(b):
         """The batch with its context: on the device (a side stream; the prefetch thread waits only
         for it) or, with --host-ctx, built on the host as the reference does."""
+        b.input_ids = b.input_ids.pin_memory()  # the loop's copies of the batch are then asynchronous
+        b.attention_mask = b.attention_mask.pin_memory()
         if a.host_ctx:
             return b, atlas.make_ctx(b.n_rows, b.valid_rows, b.tok, b.ann, device="cpu")
         return b, atlas.make_ctx_device(b.n_rows, b.valid_rows.pin_memory(), b.tok.pin_memory(),
