@@ -42,7 +42,8 @@ constexpr int kEmitHalf = 256;            // staged records per emit CTA and lis
 constexpr int kStrip = 256;               // columns per strip: one per thread of the count and emit kernels
 constexpr int kRangesMax = 64;            // row ranges per strip
 constexpr int kPartRows = 2 + kSlots;     // partial counts per (range, column): 2 poles + 16 slots
-constexpr int kU = 4;                     // rows in flight per thread in the row-major kernels
+constexpr int kU = 8;                     // rows in flight per thread in the row-major kernels
+constexpr int kChunk = 128;               // rows whose offsets and keys a row-major CTA stages at a time
 constexpr int kDenseSmemMax = 227 * 1024; // opt-in shared memory per CTA
 
 struct Lists {
@@ -184,6 +185,8 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
   using T = typename Elem<DT>::T;
   if (!triggered(count, cap, force)) return;
   __shared__ int64_t s_ceil[kSlots][kStrip];
+  __shared__ int64_t s_off[kChunk];
+  __shared__ uint32_t s_key[kChunk];
   __shared__ int s_wn[kThreads / 32];
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -209,34 +212,49 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
   int c0 = 0, c1 = 0;
   uint64_t rc[2][2] = {{0ull, 0ull}, {0ull, 0ull}};  // 16-bit counts per (pole, bin): [p][bin / 4]
   const T* Hc = H + (ok ? d : 0);
-  for (int64_t i = i0; i < i1; i += kU) {
-    T x[kU];
-    int64_t kk[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int64_t ii = i + u < i1 ? i + u : i1 - 1;  // past the range: a repeat of the last row, not counted
-      x[u] = Hc[(int64_t)rows[ii] * ld];
-      kk[u] = reservoir ? key[ii] : 0;
+  // keys lie in [0, 2^32): a ceiling of 2^32 admits every key
+  const bool mall = maxc >= (1ll << 32);
+  const uint32_t mc = mall ? 0xFFFFFFFFu : (uint32_t)maxc;
+  // the rows a chunk at a time: their offsets in H and 32-bit keys staged once per CTA (every
+  // thread reads the same rows)
+  for (int64_t cs = i0; cs < i1; cs += kChunk) {
+    const int nrow = (int)(i1 - cs < kChunk ? i1 - cs : kChunk);
+    __syncthreads();
+    if (tid < nrow) {
+      s_off[tid] = (int64_t)rows[cs + tid] * ld;
+      s_key[tid] = reservoir ? (uint32_t)key[cs + tid] : 0u;
     }
+    __syncthreads();
+    for (int j = 0; j < nrow; j += kU) {
+      T x[kU];
+      uint32_t kk[kU];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (i + u >= i1) break;
-      const float h = Elem<DT>::f(x[u]);
-      if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, i + u)) ++c0;
-      if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, i + u)) ++c1;
-      if (kk[u] < maxc) {  // maxc is 0 without a reservoir
-        if (h >= cp.e[0][0]) {
-          const int b = bin_in<NB>(h, cp.e[0]);
-          if (kk[u] < s_ceil[b][tid]) {
-            const uint64_t inc = 1ull << (16 * (b & 3));
-            if (b < 4) rc[0][0] += inc; else rc[0][1] += inc;
+      for (int u = 0; u < kU; ++u) {
+        const int jj = j + u < nrow ? j + u : nrow - 1;  // past the chunk: a repeat of its last row, not counted
+        x[u] = Hc[s_off[jj]];
+        kk[u] = s_key[jj];
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (j + u >= nrow) break;
+        const float h = Elem<DT>::f(x[u]);
+        if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, cs + j + u)) ++c0;
+        if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, cs + j + u)) ++c1;
+        if (mall || kk[u] < mc) {  // maxc is 0 without a reservoir
+          const int64_t k = (int64_t)kk[u];
+          if (h >= cp.e[0][0]) {
+            const int b = bin_in<NB>(h, cp.e[0]);
+            if (k < s_ceil[b][tid]) {
+              const uint64_t inc = 1ull << (16 * (b & 3));
+              if (b < 4) rc[0][0] += inc; else rc[0][1] += inc;
+            }
           }
-        }
-        if (-h >= cp.e[1][0]) {
-          const int b = bin_in<NB>(-h, cp.e[1]);
-          if (kk[u] < s_ceil[kMaxB + b][tid]) {
-            const uint64_t inc = 1ull << (16 * (b & 3));
-            if (b < 4) rc[1][0] += inc; else rc[1][1] += inc;
+          if (-h >= cp.e[1][0]) {
+            const int b = bin_in<NB>(-h, cp.e[1]);
+            if (k < s_ceil[kMaxB + b][tid]) {
+              const uint64_t inc = 1ull << (16 * (b & 3));
+              if (b < 4) rc[1][0] += inc; else rc[1][1] += inc;
+            }
           }
         }
       }
@@ -333,6 +351,8 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
   using T = typename Elem<DT>::T;
   if (!triggered(count, cap, force)) return;
   __shared__ int64_t s_ceil[kSlots][kStrip];
+  __shared__ int64_t s_off[kChunk];
+  __shared__ uint32_t s_key[kChunk];
   __shared__ EmitStage es;
   const int tid = threadIdx.x;
   const int strip = blockIdx.x, r = blockIdx.y, R = gridDim.y;
@@ -359,41 +379,52 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
     row_range(n_v, r, R, i0, i1);
     const T* Hc = H + (ok ? d : 0);
     const int32_t g0 = (int32_t)((layer * 2) * D + d), g1 = (int32_t)((layer * 2 + 1) * D + d);
-    for (int64_t i = i0; i < i1; i += kU) {
-      T x[kU];
-      int64_t kk[kU];
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int64_t ii = i + u < i1 ? i + u : i1 - 1;
-        x[u] = Hc[(int64_t)rows[ii] * ld];
-        kk[u] = reservoir ? key[ii] : 0;
+    const bool mall = maxc >= (1ll << 32);
+    const uint32_t mc = mall ? 0xFFFFFFFFu : (uint32_t)maxc;
+    for (int64_t cs = i0; cs < i1; cs += kChunk) {
+      const int nrow = (int)(i1 - cs < kChunk ? i1 - cs : kChunk);
+      __syncthreads();
+      if (tid < nrow) {
+        s_off[tid] = (int64_t)rows[cs + tid] * ld;
+        s_key[tid] = reservoir ? (uint32_t)key[cs + tid] : 0u;
       }
+      __syncthreads();
+      for (int j = 0; j < nrow; j += kU) {
+        T x[kU];
+        uint32_t kk[kU];
 #pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        if (i + u >= i1) break;
-        const int64_t ii = i + u;
-        const float h = Elem<DT>::f(x[u]);
-        if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, ii)) {
-          const int64_t t = tok[ii];
-          const int64_t k64 = (int64_t)((((uint64_t)key_hi(h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
-                                        0x8000000000000000ull);
-          emit_rec(es, 0, top, g0, k64, t, h, err);
+        for (int u = 0; u < kU; ++u) {
+          const int jj = j + u < nrow ? j + u : nrow - 1;
+          x[u] = Hc[s_off[jj]];
+          kk[u] = s_key[jj];
         }
-        if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, ii)) {
-          const int64_t t = tok[ii];
-          const int64_t k64 = (int64_t)((((uint64_t)key_hi(-h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
-                                        0x8000000000000000ull);
-          emit_rec(es, 0, top, g1, k64, t, -h, err);
-        }
-        const int64_t k = kk[u];
-        if (k < maxc) {  // non-direct slots have ceiling 0 here, so they never admit
-          if (h >= cp.e[0][0]) {
-            const int b = bin_in<NB>(h, cp.e[0]);
-            if (k < s_ceil[b][tid]) emit_rec(es, 1, res, g0 * B + b, -k, tok[ii], h, err);
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          if (j + u >= nrow) break;
+          const int64_t ii = cs + j + u;
+          const float h = Elem<DT>::f(x[u]);
+          if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, ii)) {
+            const int64_t t = tok[ii];
+            const int64_t k64 = (int64_t)((((uint64_t)key_hi(h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
+                                          0x8000000000000000ull);
+            emit_rec(es, 0, top, g0, k64, t, h, err);
           }
-          if (-h >= cp.e[1][0]) {
-            const int b = bin_in<NB>(-h, cp.e[1]);
-            if (k < s_ceil[kMaxB + b][tid]) emit_rec(es, 1, res, g1 * B + b, -k, tok[ii], h, err);
+          if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, ii)) {
+            const int64_t t = tok[ii];
+            const int64_t k64 = (int64_t)((((uint64_t)key_hi(-h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
+                                          0x8000000000000000ull);
+            emit_rec(es, 0, top, g1, k64, t, -h, err);
+          }
+          if (mall || kk[u] < mc) {  // non-direct slots have ceiling 0 here, so they never admit
+            const int64_t k = (int64_t)kk[u];
+            if (h >= cp.e[0][0]) {
+              const int b = bin_in<NB>(h, cp.e[0]);
+              if (k < s_ceil[b][tid]) emit_rec(es, 1, res, g0 * B + b, -k, tok[ii], h, err);
+            }
+            if (-h >= cp.e[1][0]) {
+              const int b = bin_in<NB>(-h, cp.e[1]);
+              if (k < s_ceil[kMaxB + b][tid]) emit_rec(es, 1, res, g1 * B + b, -k, tok[ii], h, err);
+            }
           }
         }
       }
@@ -744,7 +775,7 @@ int launch_dense(const void* Hv, int64_t D, int64_t ld, int64_t layer, const int
   const int64_t S = n_strips(D);
   // row ranges: about four resident 256-thread CTAs per SM over the strips, at least 64 rows and at
   // most 65535 rows (16-bit per-thread counts) per range
-  int64_t R = std::max<int64_t>(1, ((int64_t)num_sms() * 4 + S - 1) / S);
+  int64_t R = std::max<int64_t>(1, ((int64_t)num_sms() * 4) / S);  // S x R <= one resident wave
   R = std::min<int64_t>(R, std::max<int64_t>(1, n_v / 64));
   R = std::max<int64_t>(R, (n_v + 65534) / 65535);
   R = std::min<int64_t>(R, kRangesMax);
