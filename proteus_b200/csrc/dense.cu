@@ -42,7 +42,8 @@ constexpr int kEmitHalf = 256;            // staged records per emit CTA and lis
 constexpr int kStrip = 256;               // columns per strip: one per thread of the count and emit kernels
 constexpr int kRangesMax = 64;            // row ranges per strip
 constexpr int kPartRows = 2 + kSlots;     // partial counts per (range, column): 2 poles + 16 slots
-constexpr int kU = 8;                     // rows in flight per thread in the row-major kernels
+constexpr int kU = 8;                     // rows in flight per thread in the count pass
+constexpr int kUE = 4;                    // in the emit pass (its record path needs the registers)
 constexpr int kChunk = 128;               // rows whose offsets and keys a row-major CTA stages at a time
 constexpr int kDenseSmemMax = 227 * 1024; // opt-in shared memory per CTA
 
@@ -174,6 +175,50 @@ __device__ __forceinline__ void row_range(int64_t n_v, int r, int R, int64_t& i0
 }
 
 // ------------------------------------------------------------------------------------ 1. count
+// Per-pole key limits of the reservoir test: a row enters the bin search of pole p only if its key is
+// at most lim[p] = (the pole's largest ceiling) - 1 (on[p] false: no bin of the pole admits).
+__device__ __forceinline__ void pole_limits(const int64_t (*s_ceil)[kStrip], int tid, uint32_t (&lim)[2],
+                                            bool (&on)[2]) {
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    int64_t m = 0;
+#pragma unroll
+    for (int b = 0; b < kMaxB; ++b) m = s_ceil[p * kMaxB + b][tid] > m ? s_ceil[p * kMaxB + b][tid] : m;
+    on[p] = m > 0;
+    lim[p] = m > 0 ? (uint32_t)((m > (1ll << 32) ? (1ll << 32) : m) - 1) : 0u;
+  }
+}
+
+// One row of the count pass for this thread's column: admissible top-K candidates per pole, rows
+// under the ceiling of their (pole, bin).
+template <int NB>
+__device__ __forceinline__ void count_row(float h, uint32_t k, int64_t i, const ColParams& cp, const uint32_t (&lim)[2],
+                                          const bool (&on)[2], const int64_t (*s_ceil)[kStrip], int tid,
+                                          const int64_t* __restrict__ tok, int& c0, int& c1, uint64_t (&rc)[2][2]) {
+  if ((h > cp.seed[0]) | (-h > cp.seed[1])) {  // rare once seeded: one branch for both poles
+    if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, i)) ++c0;
+    if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, i)) ++c1;
+  }
+  const bool pa = on[0] & (h >= cp.e[0][0]) & (k <= lim[0]);
+  const bool pb = on[1] & (-h >= cp.e[1][0]) & (k <= lim[1]);
+  if (pa | pb) {
+    if (pa) {
+      const int b = bin_in<NB>(h, cp.e[0]);
+      if ((int64_t)k < s_ceil[b][tid]) {
+        const uint64_t inc = 1ull << (16 * (b & 3));
+        if (b < 4) rc[0][0] += inc; else rc[0][1] += inc;
+      }
+    }
+    if (pb) {
+      const int b = bin_in<NB>(-h, cp.e[1]);
+      if ((int64_t)k < s_ceil[kMaxB + b][tid]) {
+        const uint64_t inc = 1ull << (16 * (b & 3));
+        if (b < 4) rc[1][0] += inc; else rc[1][1] += inc;
+      }
+    }
+  }
+}
+
 template <int DT, int NB>
 __global__ void __launch_bounds__(kStrip, 4)
 dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
@@ -200,23 +245,18 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
   }
   ColParams cp;
   load_params(cp, ok, layer, D, d, B, K, reservoir, top_seed, top_k, E);
-  int64_t maxc = 0;  // rows whose key is at or above every ceiling of the column skip the bins
 #pragma unroll
-  for (int s = 0; s < kSlots; ++s) {
-    const int64_t c = slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed);
-    s_ceil[s][tid] = c;
-    maxc = c > maxc ? c : maxc;
-  }
+  for (int s = 0; s < kSlots; ++s) s_ceil[s][tid] = slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed);
   int64_t i0, i1;
   row_range(n_v, r, R, i0, i1);
   int c0 = 0, c1 = 0;
   uint64_t rc[2][2] = {{0ull, 0ull}, {0ull, 0ull}};  // 16-bit counts per (pole, bin): [p][bin / 4]
   const T* Hc = H + (ok ? d : 0);
-  // keys lie in [0, 2^32): a ceiling of 2^32 admits every key
-  const bool mall = maxc >= (1ll << 32);
-  const uint32_t mc = mall ? 0xFFFFFFFFu : (uint32_t)maxc;
+  uint32_t lim[2];
+  bool on[2];
+  pole_limits(s_ceil, tid, lim, on);
   // the rows a chunk at a time: their offsets in H and 32-bit keys staged once per CTA (every
-  // thread reads the same rows)
+  // thread reads the same rows); whole groups of kU rows without bounds checks, then the tail
   for (int64_t cs = i0; cs < i1; cs += kChunk) {
     const int nrow = (int)(i1 - cs < kChunk ? i1 - cs : kChunk);
     __syncthreads();
@@ -225,40 +265,21 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
       s_key[tid] = reservoir ? (uint32_t)key[cs + tid] : 0u;
     }
     __syncthreads();
-    for (int j = 0; j < nrow; j += kU) {
+    const int nfull = nrow & ~(kU - 1);
+    for (int j = 0; j < nfull; j += kU) {
       T x[kU];
       uint32_t kk[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        const int jj = j + u < nrow ? j + u : nrow - 1;  // past the chunk: a repeat of its last row, not counted
-        x[u] = Hc[s_off[jj]];
-        kk[u] = s_key[jj];
+        x[u] = Hc[s_off[j + u]];
+        kk[u] = s_key[j + u];
       }
 #pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        if (j + u >= nrow) break;
-        const float h = Elem<DT>::f(x[u]);
-        if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, cs + j + u)) ++c0;
-        if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, cs + j + u)) ++c1;
-        if (mall || kk[u] < mc) {  // maxc is 0 without a reservoir
-          const int64_t k = (int64_t)kk[u];
-          if (h >= cp.e[0][0]) {
-            const int b = bin_in<NB>(h, cp.e[0]);
-            if (k < s_ceil[b][tid]) {
-              const uint64_t inc = 1ull << (16 * (b & 3));
-              if (b < 4) rc[0][0] += inc; else rc[0][1] += inc;
-            }
-          }
-          if (-h >= cp.e[1][0]) {
-            const int b = bin_in<NB>(-h, cp.e[1]);
-            if (k < s_ceil[kMaxB + b][tid]) {
-              const uint64_t inc = 1ull << (16 * (b & 3));
-              if (b < 4) rc[1][0] += inc; else rc[1][1] += inc;
-            }
-          }
-        }
-      }
+      for (int u = 0; u < kU; ++u)
+        count_row<NB>(Elem<DT>::f(x[u]), kk[u], cs + j + u, cp, lim, on, s_ceil, tid, tok, c0, c1, rc);
     }
+    for (int j = nfull; j < nrow; ++j)
+      count_row<NB>(Elem<DT>::f(Hc[s_off[j]]), s_key[j], cs + j, cp, lim, on, s_ceil, tid, tok, c0, c1, rc);
   }
   if (ok) {
     int32_t* P = ws.part + (int64_t)r * kPartRows * D + d;
@@ -340,6 +361,40 @@ __device__ __forceinline__ void emit_rec(EmitStage& es, int w, const Lists& o, i
   }
 }
 
+// One row of the emit pass for this thread's column: the records of its direct poles and bins.
+template <int NB>
+__device__ __forceinline__ void emit_row(float h, uint32_t k, int64_t i, const ColParams& cp, const uint32_t (&lim)[2],
+                                         const bool (&on)[2], const int64_t (*s_ceil)[kStrip], int tid,
+                                         const int64_t* __restrict__ tok, int32_t g0, int32_t g1, int B, EmitStage& es,
+                                         const Lists& top, const Lists& res, int32_t* __restrict__ err) {
+  if ((h > cp.seed[0]) | (-h > cp.seed[1])) {
+    if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, i)) {
+      const int64_t t = tok[i];
+      emit_rec(es, 0, top, g0,
+               (int64_t)((((uint64_t)key_hi(h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^ 0x8000000000000000ull), t,
+               h, err);
+    }
+    if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, i)) {
+      const int64_t t = tok[i];
+      emit_rec(es, 0, top, g1,
+               (int64_t)((((uint64_t)key_hi(-h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^ 0x8000000000000000ull), t,
+               -h, err);
+    }
+  }
+  const bool pa = on[0] & (h >= cp.e[0][0]) & (k <= lim[0]);
+  const bool pb = on[1] & (-h >= cp.e[1][0]) & (k <= lim[1]);
+  if (pa | pb) {  // non-direct slots have ceiling 0 here, so they never admit
+    if (pa) {
+      const int b = bin_in<NB>(h, cp.e[0]);
+      if ((int64_t)k < s_ceil[b][tid]) emit_rec(es, 1, res, g0 * B + b, -(int64_t)k, tok[i], h, err);
+    }
+    if (pb) {
+      const int b = bin_in<NB>(-h, cp.e[1]);
+      if ((int64_t)k < s_ceil[kMaxB + b][tid]) emit_rec(es, 1, res, g1 * B + b, -(int64_t)k, tok[i], h, err);
+    }
+  }
+}
+
 template <int DT, int NB>
 __global__ void __launch_bounds__(kStrip, 4)
 dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t ld, const int32_t* __restrict__ rows,
@@ -364,13 +419,12 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
   load_params(cp, ok, layer, D, d, B, K, reservoir, top_seed, top_k, E);
   if (th & 1u) cp.seed[0] = __int_as_float(0x7F800000);  // pole emitted by the hard-column kernel
   if (th & 2u) cp.seed[1] = __int_as_float(0x7F800000);
-  int64_t maxc = 0;  // the largest ceiling of the direct slots (0: no reservoir record here)
 #pragma unroll
-  for (int s = 0; s < kSlots; ++s) {
-    const int64_t c = ((direct >> s) & 1u) ? slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed) : 0;
-    s_ceil[s][tid] = c;
-    maxc = c > maxc ? c : maxc;
-  }
+  for (int s = 0; s < kSlots; ++s)  // ceilings of the direct slots only (0: the slot admits nothing here)
+    s_ceil[s][tid] = ((direct >> s) & 1u) ? slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed) : 0;
+  uint32_t lim[2];
+  bool on[2];
+  pole_limits(s_ceil, tid, lim, on);
   if (tid < 2) es.n[tid] = 0;
   __syncthreads();
   const bool any = __syncthreads_or(ok && (((th & 3u) != 3u) || direct != 0)) != 0;
@@ -379,8 +433,6 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
     row_range(n_v, r, R, i0, i1);
     const T* Hc = H + (ok ? d : 0);
     const int32_t g0 = (int32_t)((layer * 2) * D + d), g1 = (int32_t)((layer * 2 + 1) * D + d);
-    const bool mall = maxc >= (1ll << 32);
-    const uint32_t mc = mall ? 0xFFFFFFFFu : (uint32_t)maxc;
     for (int64_t cs = i0; cs < i1; cs += kChunk) {
       const int nrow = (int)(i1 - cs < kChunk ? i1 - cs : kChunk);
       __syncthreads();
@@ -389,45 +441,23 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
         s_key[tid] = reservoir ? (uint32_t)key[cs + tid] : 0u;
       }
       __syncthreads();
-      for (int j = 0; j < nrow; j += kU) {
-        T x[kU];
-        uint32_t kk[kU];
+      const int nfull = nrow & ~(kUE - 1);
+      for (int j = 0; j < nfull; j += kUE) {
+        T x[kUE];
+        uint32_t kk[kUE];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int jj = j + u < nrow ? j + u : nrow - 1;
-          x[u] = Hc[s_off[jj]];
-          kk[u] = s_key[jj];
+        for (int u = 0; u < kUE; ++u) {
+          x[u] = Hc[s_off[j + u]];
+          kk[u] = s_key[j + u];
         }
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          if (j + u >= nrow) break;
-          const int64_t ii = cs + j + u;
-          const float h = Elem<DT>::f(x[u]);
-          if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, ii)) {
-            const int64_t t = tok[ii];
-            const int64_t k64 = (int64_t)((((uint64_t)key_hi(h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
-                                          0x8000000000000000ull);
-            emit_rec(es, 0, top, g0, k64, t, h, err);
-          }
-          if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, ii)) {
-            const int64_t t = tok[ii];
-            const int64_t k64 = (int64_t)((((uint64_t)key_hi(-h) << 32) | (uint64_t)(kM32 - (uint32_t)t)) ^
-                                          0x8000000000000000ull);
-            emit_rec(es, 0, top, g1, k64, t, -h, err);
-          }
-          if (mall || kk[u] < mc) {  // non-direct slots have ceiling 0 here, so they never admit
-            const int64_t k = (int64_t)kk[u];
-            if (h >= cp.e[0][0]) {
-              const int b = bin_in<NB>(h, cp.e[0]);
-              if (k < s_ceil[b][tid]) emit_rec(es, 1, res, g0 * B + b, -k, tok[ii], h, err);
-            }
-            if (-h >= cp.e[1][0]) {
-              const int b = bin_in<NB>(-h, cp.e[1]);
-              if (k < s_ceil[kMaxB + b][tid]) emit_rec(es, 1, res, g1 * B + b, -k, tok[ii], h, err);
-            }
-          }
-        }
+        for (int u = 0; u < kUE; ++u)
+          emit_row<NB>(Elem<DT>::f(x[u]), kk[u], cs + j + u, cp, lim, on, s_ceil, tid, tok, g0, g1, B, es, top, res,
+                       err);
       }
+      for (int j = nfull; j < nrow; ++j)
+        emit_row<NB>(Elem<DT>::f(Hc[s_off[j]]), s_key[j], cs + j, cp, lim, on, s_ceil, tid, tok, g0, g1, B, es, top,
+                     res, err);
     }
   }
   __syncthreads();
