@@ -175,32 +175,67 @@ __device__ __forceinline__ void row_range(int64_t n_v, int r, int R, int64_t& i0
 }
 
 // ------------------------------------------------------------------------------------ 1. count
-// Per-pole key limits of the reservoir test: a row enters the bin search of pole p only if its key is
-// at most lim[p] = (the pole's largest ceiling) - 1 (on[p] false: no bin of the pole admits).
-__device__ __forceinline__ void pole_limits(const int64_t (*s_ceil)[kStrip], int tid, uint32_t (&lim)[2],
-                                            bool (&on)[2]) {
+// Necessary condition for a row to enter the bin search of pole p (value s = +-h, key k), kept in
+// registers per thread: either s reaches the top bin's edge and k is under the top bin's ceiling, or
+// s reaches the lowest edge and k is under the largest ceiling of the other bins. The top bin (the
+// rarest values) is the one whose reservoir stays open longest, often with the whole key range as its
+// ceiling; apart from it, seeded ceilings are small, so most rows fail both tests without a search.
+struct PoleGate {
+  float etop[2];                   // edge of the top bin (bin B-1)
+  uint32_t lim_top[2], lim_rest[2];  // ceiling - 1 of the top bin / largest ceiling - 1 of the others
+  bool on_top[2], on_rest[2];      // a ceiling above 0 exists
+};
+
+__device__ __forceinline__ uint32_t ceil_limit(int64_t c) {
+  return c > 0 ? (uint32_t)((c > (1ll << 32) ? (1ll << 32) : c) - 1) : 0u;
+}
+
+// NB < kMaxB: compiled for exactly NB bins (B == NB), so the top bin's index is a constant and the
+// edges stay in registers.
+template <int NB>
+__device__ __forceinline__ void pole_gate(const int64_t (*s_ceil)[kStrip], int tid, int B, const ColParams& cp,
+                                          PoleGate& g) {
+  const int tb = NB < kMaxB ? NB - 1 : B - 1;
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
-    int64_t m = 0;
+    int64_t rest = 0, top = 0;
+    float et = __int_as_float(0x7FC00000);
 #pragma unroll
-    for (int b = 0; b < kMaxB; ++b) m = s_ceil[p * kMaxB + b][tid] > m ? s_ceil[p * kMaxB + b][tid] : m;
-    on[p] = m > 0;
-    lim[p] = m > 0 ? (uint32_t)((m > (1ll << 32) ? (1ll << 32) : m) - 1) : 0u;
+    for (int b = 0; b < kMaxB; ++b) {
+      const int64_t c = s_ceil[p * kMaxB + b][tid];
+      if (b == tb) {
+        top = c;
+        et = cp.e[p][b];
+      } else if (b < tb) {
+        rest = c > rest ? c : rest;
+      }
+    }
+    g.etop[p] = et;
+    g.on_top[p] = top > 0;
+    g.lim_top[p] = ceil_limit(top);
+    g.on_rest[p] = rest > 0;
+    g.lim_rest[p] = ceil_limit(rest);
   }
+}
+
+template <int P>
+__device__ __forceinline__ bool gate_pass(float s, uint32_t k, const ColParams& cp, const PoleGate& g) {
+  return (g.on_top[P] & (s >= g.etop[P]) & (k <= g.lim_top[P])) |
+         (g.on_rest[P] & (s >= cp.e[P][0]) & (k <= g.lim_rest[P]));
 }
 
 // One row of the count pass for this thread's column: admissible top-K candidates per pole, rows
 // under the ceiling of their (pole, bin).
 template <int NB>
-__device__ __forceinline__ void count_row(float h, uint32_t k, int64_t i, const ColParams& cp, const uint32_t (&lim)[2],
-                                          const bool (&on)[2], const int64_t (*s_ceil)[kStrip], int tid,
+__device__ __forceinline__ void count_row(float h, uint32_t k, int64_t i, const ColParams& cp, const PoleGate& gt,
+                                          const int64_t (*s_ceil)[kStrip], int tid,
                                           const int64_t* __restrict__ tok, int& c0, int& c1, uint64_t (&rc)[2][2]) {
   if ((h > cp.seed[0]) | (-h > cp.seed[1])) {  // rare once seeded: one branch for both poles
     if (h > cp.seed[0] && top_above(h, cp.ku[0], tok, i)) ++c0;
     if (-h > cp.seed[1] && top_above(-h, cp.ku[1], tok, i)) ++c1;
   }
-  const bool pa = on[0] & (h >= cp.e[0][0]) & (k <= lim[0]);
-  const bool pb = on[1] & (-h >= cp.e[1][0]) & (k <= lim[1]);
+  const bool pa = gate_pass<0>(h, k, cp, gt);
+  const bool pb = gate_pass<1>(-h, k, cp, gt);
   if (pa | pb) {
     if (pa) {
       const int b = bin_in<NB>(h, cp.e[0]);
@@ -252,9 +287,8 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
   int c0 = 0, c1 = 0;
   uint64_t rc[2][2] = {{0ull, 0ull}, {0ull, 0ull}};  // 16-bit counts per (pole, bin): [p][bin / 4]
   const T* Hc = H + (ok ? d : 0);
-  uint32_t lim[2];
-  bool on[2];
-  pole_limits(s_ceil, tid, lim, on);
+  PoleGate gt;
+  pole_gate<NB>(s_ceil, tid, B, cp, gt);
   // the rows a chunk at a time: their offsets in H and 32-bit keys staged once per CTA (every
   // thread reads the same rows); whole groups of kU rows without bounds checks, then the tail
   for (int64_t cs = i0; cs < i1; cs += kChunk) {
@@ -276,10 +310,10 @@ dense_count_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_
       }
 #pragma unroll
       for (int u = 0; u < kU; ++u)
-        count_row<NB>(Elem<DT>::f(x[u]), kk[u], cs + j + u, cp, lim, on, s_ceil, tid, tok, c0, c1, rc);
+        count_row<NB>(Elem<DT>::f(x[u]), kk[u], cs + j + u, cp, gt, s_ceil, tid, tok, c0, c1, rc);
     }
     for (int j = nfull; j < nrow; ++j)
-      count_row<NB>(Elem<DT>::f(Hc[s_off[j]]), s_key[j], cs + j, cp, lim, on, s_ceil, tid, tok, c0, c1, rc);
+      count_row<NB>(Elem<DT>::f(Hc[s_off[j]]), s_key[j], cs + j, cp, gt, s_ceil, tid, tok, c0, c1, rc);
   }
   if (ok) {
     int32_t* P = ws.part + (int64_t)r * kPartRows * D + d;
@@ -363,8 +397,8 @@ __device__ __forceinline__ void emit_rec(EmitStage& es, int w, const Lists& o, i
 
 // One row of the emit pass for this thread's column: the records of its direct poles and bins.
 template <int NB>
-__device__ __forceinline__ void emit_row(float h, uint32_t k, int64_t i, const ColParams& cp, const uint32_t (&lim)[2],
-                                         const bool (&on)[2], const int64_t (*s_ceil)[kStrip], int tid,
+__device__ __forceinline__ void emit_row(float h, uint32_t k, int64_t i, const ColParams& cp, const PoleGate& gt,
+                                         const int64_t (*s_ceil)[kStrip], int tid,
                                          const int64_t* __restrict__ tok, int32_t g0, int32_t g1, int B, EmitStage& es,
                                          const Lists& top, const Lists& res, int32_t* __restrict__ err) {
   if ((h > cp.seed[0]) | (-h > cp.seed[1])) {
@@ -381,8 +415,8 @@ __device__ __forceinline__ void emit_row(float h, uint32_t k, int64_t i, const C
                -h, err);
     }
   }
-  const bool pa = on[0] & (h >= cp.e[0][0]) & (k <= lim[0]);
-  const bool pb = on[1] & (-h >= cp.e[1][0]) & (k <= lim[1]);
+  const bool pa = gate_pass<0>(h, k, cp, gt);
+  const bool pb = gate_pass<1>(-h, k, cp, gt);
   if (pa | pb) {  // non-direct slots have ceiling 0 here, so they never admit
     if (pa) {
       const int b = bin_in<NB>(h, cp.e[0]);
@@ -422,9 +456,8 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
 #pragma unroll
   for (int s = 0; s < kSlots; ++s)  // ceilings of the direct slots only (0: the slot admits nothing here)
     s_ceil[s][tid] = ((direct >> s) & 1u) ? slot_ceiling(s, ok, layer, D, d, B, Kr, reservoir, res_s, res_seed) : 0;
-  uint32_t lim[2];
-  bool on[2];
-  pole_limits(s_ceil, tid, lim, on);
+  PoleGate gt;
+  pole_gate<NB>(s_ceil, tid, B, cp, gt);
   if (tid < 2) es.n[tid] = 0;
   __syncthreads();
   const bool any = __syncthreads_or(ok && (((th & 3u) != 3u) || direct != 0)) != 0;
@@ -452,11 +485,11 @@ dense_emit_kernel(const typename Elem<DT>::T* __restrict__ H, int64_t D, int64_t
         }
 #pragma unroll
         for (int u = 0; u < kUE; ++u)
-          emit_row<NB>(Elem<DT>::f(x[u]), kk[u], cs + j + u, cp, lim, on, s_ceil, tid, tok, g0, g1, B, es, top, res,
+          emit_row<NB>(Elem<DT>::f(x[u]), kk[u], cs + j + u, cp, gt, s_ceil, tid, tok, g0, g1, B, es, top, res,
                        err);
       }
       for (int j = nfull; j < nrow; ++j)
-        emit_row<NB>(Elem<DT>::f(Hc[s_off[j]]), s_key[j], cs + j, cp, lim, on, s_ceil, tid, tok, g0, g1, B, es, top,
+        emit_row<NB>(Elem<DT>::f(Hc[s_off[j]]), s_key[j], cs + j, cp, gt, s_ceil, tid, tok, g0, g1, B, es, top,
                      res, err);
     }
   }
