@@ -32,6 +32,25 @@ def test_argument_errors_are_reported_without_a_gpu():
     assert rc == 1 and b"K must be" in lib.atlas_last_error()
 
 
+def test_dense_select_rejects_out_of_range_shapes_on_the_host():
+    """atlas_dense_select checks its limits before any CUDA call: 1..8 bins, K and Kr up to 256, the
+    staging bound 2K + 2*B*Kr <= 1024, at most 64 x 65535 valid rows (16-bit per-thread counts over
+    at most 64 row ranges) and at most 65536 columns (256 strips of 256)."""
+    lib = _lib.load()
+
+    def call(T=1000, D=512, n_v=1000, B=5, K=100, Kr=32):
+        args = [None, 1, T, D, D, 0, None, n_v, None, None, None, B, K, Kr, 1] + [None] * 6 + [0, 1] + \
+               [None] * 5 + [0] + [None] * 5 + [0, None, 0, None, None, None]
+        return lib.atlas_dense_select(*args)
+
+    assert call(B=9) == 1 and b"B must be" in lib.atlas_last_error()
+    assert call(K=300) == 1
+    assert call(K=200, Kr=100) == 1 and b"staging area" in lib.atlas_last_error()
+    assert call(T=64 * 65535 + 1, n_v=64 * 65535 + 1) == 1 and b"valid rows" in lib.atlas_last_error()
+    assert call(D=65536 + 256) == 1 and b"D above" in lib.atlas_last_error()
+    assert call(n_v=2000) == 1 and b"bad shape" in lib.atlas_last_error()  # more valid rows than rows
+
+
 def test_workspace_size_queries():
     lib = _lib.load()
     assert lib.atlas_merge_ws_i32(4096, 100) >= 4 * 4096
